@@ -1,0 +1,316 @@
+"""Benchmark: one EraserDiT self-attention layer at 2 x 32640 tokens on B200.
+
+Metric: "DiT self-attn layer ms & TFLOP/s @2x32640 tok,
+1/2/4/8 B200 (% of peak)".  One step = one full layer (QKV projection, fused
+QK RMSNorm + RoPE, attention, output projection; at N > 1 the Ulysses
+all-to-all exchanges as well) over B=2 x 32640 synthetic tokens (N(0, 1)
+hidden states, N(0, 0.02) weights, seed 1).  ``value`` is whole-job TFLOP/s
+(19.645 TFLOP per layer / max-over-ranks step time).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+BATCH, FRAMES, HEIGHT, WIDTH = 2, 16, 34, 60
+SEQ = FRAMES * HEIGHT * WIDTH
+HIDDEN, HEADS, HEAD_DIM = 2048, 32, 64
+EPS = 1e-6
+LINEAR_FLOP = 4 * 2 * BATCH * SEQ * HIDDEN * HIDDEN
+ATTN_FLOP = 4 * BATCH * HEADS * SEQ * SEQ * HEAD_DIM
+LAYER_FLOP = LINEAR_FLOP + ATTN_FLOP
+METRIC = "DiT self-attn layer ms & TFLOP/s @2x32640 tok, 1/2/4/8 B200 (% of peak)"
+UNIT = "TFLOP/s"
+WORKLOAD = ("config 1: one DiT self-attention layer (QKV proj, QK RMSNorm, 3D RoPE, "
+            "SDPA, out proj), B=2 (CFG stacked) x 32640 tokens (16x34x60), "
+            "hidden 2048, 32x64 heads, BF16")
+
+
+def log(msg: str) -> None:
+    print(msg, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------ helpers
+def measured_peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def profiled_traffic(kernel: str) -> float | None:
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    path = ROOT / "profiles" / f"{kernel}.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.index)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self) -> dict:
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        sm, mx, reasons = [], [], set()
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for name, value in zip(names, r[5:9]):
+                if value.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- CPU sample
+def cpu_sample_step(threads: int):
+    """1/64 of the config-1 layer through the oracle (the reference's CPU path):
+    the four projections for 510 of the 65280 tokens, their QK RMSNorm + RoPE,
+    and one (batch, head) of attention over the full 32640-token sequence."""
+    from oracle import reference_path as ref
+    torch.set_num_threads(threads)
+    rows = BATCH * SEQ // 64
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(1, rows, HIDDEN, generator=g)
+    w = [torch.randn(HIDDEN, HIDDEN, generator=g) * 0.02 for _ in range(4)]
+    b = torch.zeros(HIDDEN)
+    ones = torch.ones(HIDDEN)
+    cos, sin = ref.rope_table(1, FRAMES, HEIGHT, WIDTH)
+    cos, sin = cos[:, :rows], sin[:, :rows]
+    qh, kh, vh = (torch.randn(1, SEQ, 1, HEAD_DIM, generator=g) for _ in range(3))
+    flop = 4 * 2 * rows * HIDDEN * HIDDEN + 4 * SEQ * SEQ * HEAD_DIM
+
+    def step():
+        with torch.no_grad():
+            q = ref.rms_norm(torch.nn.functional.linear(x, w[0], b), ones, EPS)
+            k = ref.rms_norm(torch.nn.functional.linear(x, w[1], b), ones, EPS)
+            v = torch.nn.functional.linear(x, w[2], b)
+            q, k = ref.apply_rotary_emb(q, cos, sin), ref.apply_rotary_emb(k, cos, sin)
+            core = ref.sdpa_bshd(qh, kh, vh, 0.125)
+            torch.nn.functional.linear(v, w[3], b)
+        return core
+    return step, flop, (f"1/64 of the layer: projections + QK norm/RoPE for {rows} tokens and one "
+                        f"(batch, head) of fp32 SDPA over {SEQ} tokens")
+
+
+def cpu_baseline(steps: int = 3) -> dict:
+    threads = os.cpu_count() or 1
+    step, flop, sample = cpu_sample_step(threads)
+    step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = (time.perf_counter() - t0) / steps
+    return {"value": flop / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": sample + f"; {steps} timed steps of {dt:.2f} s"}
+
+
+def run_reference(args, rank: int) -> None:
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    step, flop, sample = cpu_sample_step(threads)
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    value = flop / dt / 1e12
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": BATCH, "seq_len": SEQ,
+                   "parallelism": "cpu", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ------------------------------------------------------------ GPU arm
+def build_problem(device):
+    from eraserdit_b200.layer import EraserDiTSelfAttention
+    from eraserdit_b200.rotary import LTXVideoRotaryPosEmbed
+    from oracle.inputs import make_params  # seeded synthetic weights (same generator as tests)
+    params = make_params(1, EPS, device=device)
+    layer = EraserDiTSelfAttention.from_params(params.to(torch.bfloat16), device=device)
+    rope = LTXVideoRotaryPosEmbed()(FRAMES, HEIGHT, WIDTH, device=device)
+    return layer, rope
+
+
+def run_single(args) -> None:
+    from eraserdit_b200 import _native
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    layer, rope = build_problem(device)
+    g = torch.Generator(device=device).manual_seed(1)
+    x = torch.randn(BATCH, SEQ, HIDDEN, generator=g, device=device).bfloat16()
+    stream = torch.cuda.current_stream(device)
+    attn_events = []
+
+    from eraserdit_b200.attention import attention_bshd
+    from eraserdit_b200.operator_fusion import qk_norm_rope_into
+    attn_out = torch.empty(BATCH, SEQ, HIDDEN, device=device, dtype=torch.bfloat16)
+
+    def step(record: bool):
+        # Same calls as EraserDiTSelfAttention.forward, with CUDA events around
+        # the attention kernel alone (on the stream it is launched on).
+        qkv = layer.project_qkv(x)
+        q, k, v = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN], qkv[..., 2 * HIDDEN:]
+        qk_norm_rope_into(q, k, layer.norm_q, layer.norm_k, layer.eps, rope, q, k)
+        if record:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        attention_bshd(q.unflatten(2, (HEADS, HEAD_DIM)), k.unflatten(2, (HEADS, HEAD_DIM)),
+                       v.unflatten(2, (HEADS, HEAD_DIM)), layer.softmax_scale,
+                       out=attn_out.unflatten(2, (HEADS, HEAD_DIM)))
+        if record:
+            e1.record(stream)
+            attn_events.append((e0, e1))
+        return layer.project_out(attn_out)
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            y = step(True)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    core_ms = statistics.mean(a.elapsed_time(b) for a, b in attn_events)
+    status = _native.read_status(device)
+    if status:
+        raise RuntimeError(f"kernel wait timed out (status {status})")
+    del y
+
+    # End to end through the public API: pinned host input -> layer -> pinned host output.
+    host_x = x.cpu().pin_memory()
+    host_y = torch.empty(BATCH, SEQ, HIDDEN, dtype=torch.bfloat16).pin_memory()
+    for _ in range(max(args.warmup, 1)):
+        host_y.copy_(layer(host_x.to(device, non_blocking=True), rope), non_blocking=True)
+    torch.cuda.synchronize()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        host_y.copy_(layer(host_x.to(device, non_blocking=True), rope), non_blocking=True)
+    e_stop.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e_start.elapsed_time(e_stop) / args.steps
+
+    peaks, peak_src = measured_peaks()
+    timed_s = ms * args.steps / 1e3
+    peak_key = "bf16_tflops_sustained" if timed_s >= 1.0 else "bf16_tflops"
+    achieved = ATTN_FLOP / (core_ms / 1e3) / 1e12
+    clock = clocks.summary()
+    line = {
+        "metric": METRIC, "value": LAYER_FLOP / (ms / 1e3) / 1e12, "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "global_batch": BATCH, "seq_len": SEQ,
+                   "parallelism": "sp1",
+                   "l2": "inputs larger than L2 (x 267 MB, QKV 802 MB per step)"},
+        "layer_tflop": LAYER_FLOP / 1e12,
+        "roofline": {"kernel": "attn_fwd_bf16", "bound": "tensor",
+                     "achieved": achieved, "peak": peaks[peak_key], "unit": UNIT,
+                     "frac": achieved / peaks[peak_key],
+                     "peak_source": f"{peak_src} {peak_key}",
+                     "traffic": profiled_traffic("attn_fwd_bf16_config1"),
+                     "kernel_ms": core_ms},
+        "e2e": {"value": LAYER_FLOP / (e2e_ms / 1e3) / 1e12, "unit": UNIT,
+                "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": host_x.numel() * host_x.element_size(),
+                "d2h_bytes_per_step": host_y.numel() * host_y.element_size()},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clock,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline()
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", default="native", choices=["native", "reference"])
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if args.gpus == 1 and int(os.environ.get("WORLD_SIZE", "1")) == 1:
+        run_single(args)
+        return
+    from eraserdit_b200.bench_sp import run_sequence_parallel
+    run_sequence_parallel(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,103 @@
+"""ctypes binding of ``liberaserdit_b200.so`` (declared in ``include/eraserdit_b200.h``).
+
+The library is the only compute path: if it is missing or cannot be loaded,
+every entry point raises.  There is no CPU or PyTorch fallback.
+
+Tensors are passed as raw device pointers with element strides, on the
+caller's current CUDA stream, in the style of the reference's mask-STA ctypes
+binding (``layers/attention/backends/mask_sta.py:108-131``): a nonzero return
+code raises ``RuntimeError``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+LIBRARY_PATH = Path(__file__).resolve().parent / "liberaserdit_b200.so"
+ABI_VERSION = 1
+
+_c_int, _c_i64, _c_float, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
+
+# name -> argument types, in header order.
+SIGNATURES = {
+    "erd_abi_version": [],
+    "erd_error_string": [_c_int],
+    "erd_rope_axis_table": [_vp, _c_int, _c_int, _c_int, _c_int, _c_int, _c_float, _c_float,
+                            _c_float, _c_float, _c_float, _c_float, _c_float, _c_float, _vp, _vp],
+    "erd_qk_norm_rope": [_vp, _vp, _vp, _c_i64, _c_i64, _c_int, _c_int, _c_int, _vp, _vp,
+                         _c_float, _c_int, _vp, _vp, _c_i64, _c_i64, _vp, _c_int, _c_int, _c_int,
+                         _c_int, _c_int, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_i64,
+                         _vp],
+    "erd_attn_fwd_bf16": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 5 + [_c_float, _vp]
+                         + [_c_i64] * 4 + [_vp, _vp],
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    """Load the library once; raise if it is absent or of another ABI version."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = Path(os.environ.get("ERASERDIT_B200_LIBRARY", LIBRARY_PATH))
+        if not path.exists():
+            raise RuntimeError(
+                f"eraserdit_b200 CUDA library not found at {path}; build it with "
+                "`python -m eraserdit_b200.csrc.build` (no fallback path exists)")
+        lib = ctypes.CDLL(str(path))
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = ctypes.c_char_p if name == "erd_error_string" else ctypes.c_int
+        if lib.erd_abi_version() != ABI_VERSION:
+            raise RuntimeError(
+                f"eraserdit_b200 ABI mismatch: library {lib.erd_abi_version()}, "
+                f"binding {ABI_VERSION}")
+        _lib = lib
+    return _lib
+
+
+def check(code: int, what: str) -> None:
+    if code != 0:
+        message = load().erd_error_string(code).decode()
+        raise RuntimeError(f"{what} failed ({code}): {message}")
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+_status: dict[int, torch.Tensor] = {}
+
+
+def status_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32 word that kernels set when a bounded wait gives up."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    word = _status.get(index)
+    if word is None:
+        word = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
+        _status[index] = word
+    return word
+
+
+def read_status(device: torch.device, reset: bool = True) -> int:
+    """Synchronise and return the device status bits (0 = no kernel timed out)."""
+    word = status_word(device)
+    value = int(word.item())
+    if reset and value:
+        word.zero_()
+    return value
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()

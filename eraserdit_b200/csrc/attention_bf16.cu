@@ -1,0 +1,478 @@
+// Non-causal, unmasked scaled-dot-product attention for head_dim 64 on sm_100a.
+//
+// Replaces the SDPA call of the reference's self-attention path
+// (layers/attention/backends/sdpa.py:56-80, called from
+// models/dits/eraserdit_attention.py:287-289): out = softmax(Q K^T * scale) V
+// per (batch, head), BF16 in / BF16 out, FP32 softmax state and accumulation.
+//
+// Design (one CTA per pair of 128-row query tiles of one (batch, head)):
+//   warp 8      TMA producer: Q pair once, then K / V tiles through a ring of
+//               shared-memory stages (128 x 64 BF16, 128-byte swizzle).
+//   warp 9      MMA issuer (one thread): S = Q K^T into TMEM (M=128, N=128,
+//               K=64), then O += P V with P read from TMEM (M=128, N=64, K=128).
+//   warps 0-7   two softmax warpgroups, one per query tile; thread r owns
+//               query row r: reads its S row from TMEM, keeps the running
+//               max / sum, writes P (BF16) to TMEM, rescales its O row when
+//               the running max grows by more than 2^8, and finally writes
+//               O / l to global memory.
+// TMEM columns: S_A [0,128) S_B [128,256) O_A [256,320) O_B [320,384)
+//               P_A [384,448) P_B [448,512).
+//
+// The key / value sequence may be split into `nseg` segments of `seg_len`
+// tokens each (the layout the Ulysses all-to-all delivers: one segment per
+// source rank).  Tiles never straddle a segment; the last tile of a segment
+// is zero-filled by TMA and its missing columns are masked.  Queries use the
+// same tiling, and output rows are scattered back with the caller's strides.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <math_constants.h>
+
+#include "host_common.h"
+#include "sm100_ptx.cuh"
+#include "tmem_io.cuh"
+
+namespace erd {
+
+constexpr int kBlockM = 128;  // query rows per tile
+constexpr int kBlockN = 128;  // key / value rows per tile
+constexpr int kHeadDim = 64;
+constexpr int kStages = 3;  // K and V ring depth
+constexpr int kTileBytes = kBlockM * kHeadDim * 2;  // 16 KB
+constexpr int kThreads = 320;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only if max grows > 2^8
+
+struct AttnParams {
+  int seg_len;
+  int nseg;
+  int tiles_per_seg;
+  int q_tiles;
+  float scale_log2;
+  __nv_bfloat16* out;
+  long long o_rs, o_hs, o_bs, o_ss;
+  int* status;
+};
+
+struct __align__(8) AttnBarriers {
+  uint64_t q_full;
+  uint64_t k_full[kStages];
+  uint64_t k_empty[kStages];
+  uint64_t v_full[kStages];
+  uint64_t v_empty[kStages];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_done[2];
+  uint64_t mma_drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+constexpr int kSmemQ = 0;
+constexpr int kSmemK = kSmemQ + 2 * kTileBytes;
+constexpr int kSmemV = kSmemK + kStages * kTileBytes;
+constexpr int kSmemBar = kSmemV + kStages * kTileBytes;
+constexpr int kSmemBytes = kSmemBar + 1024;
+// +1024 for aligning the dynamic shared memory base to the swizzle atom.
+constexpr int kSmemLaunchBytes = kSmemBytes + 1024;
+static_assert(kSmemLaunchBytes <= 227 * 1024, "shared memory budget");
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_per_seg, int& seg, int& l0) {
+  seg = tile / tiles_per_seg;
+  l0 = (tile - seg * tiles_per_seg) * kBlockN;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                         const __grid_constant__ CUtensorMap tmap_k,
+                         const __grid_constant__ CUtensorMap tmap_v, const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  AttnBarriers* bars = reinterpret_cast<AttnBarriers*>(smem + kSmemBar);
+  const uint32_t sQ = smem_u32(smem + kSmemQ);
+  const uint32_t sK = smem_u32(smem + kSmemK);
+  const uint32_t sV = smem_u32(smem + kSmemV);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int pair = blockIdx.x;
+  const int head = blockIdx.y;
+  const int batch = blockIdx.z;
+  const int n_kv = p.q_tiles;  // the same tiling is used for keys and queries
+  volatile int* abort = &bars->abort;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bars->q_full), 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&bars->k_full[s]), 1);
+      mbar_init(smem_u32(&bars->k_empty[s]), 1);
+      mbar_init(smem_u32(&bars->v_full[s]), 1);
+      mbar_init(smem_u32(&bars->v_empty[s]), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(smem_u32(&bars->s_full[t]), 1);
+      mbar_init(smem_u32(&bars->p_full[t]), kBlockM);
+      mbar_init(smem_u32(&bars->o_done[t]), 1);
+    }
+    mbar_init(smem_u32(&bars->mma_drain), 1);
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 8) {
+    tmem_alloc(smem_u32(&bars->tmem_base), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_q);
+      tma_prefetch_desc(&tmap_k);
+      tma_prefetch_desc(&tmap_v);
+      int qa = 2 * pair, qb = 2 * pair + 1;
+      if (qb >= p.q_tiles) qb = qa;
+      int seg, l0;
+      const uint32_t qbar = smem_u32(&bars->q_full);
+      mbar_arrive_expect_tx(qbar, 2 * kTileBytes);
+      tile_coords(qa, p.tiles_per_seg, seg, l0);
+      tma_load_5d(sQ, &tmap_q, qbar, 0, l0, head, batch, seg);
+      tile_coords(qb, p.tiles_per_seg, seg, l0);
+      tma_load_5d(sQ + kTileBytes, &tmap_q, qbar, 0, l0, head, batch, seg);
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        tile_coords(j, p.tiles_per_seg, seg, l0);
+        if (!mbar_wait(smem_u32(&bars->k_empty[s]), ph ^ 1, abort, p.status,
+                       kStatusTimeoutProducer))
+          break;
+        mbar_arrive_expect_tx(smem_u32(&bars->k_full[s]), kTileBytes);
+        tma_load_5d(sK + s * kTileBytes, &tmap_k, smem_u32(&bars->k_full[s]), 0, l0, head, batch,
+                    seg);
+        if (!mbar_wait(smem_u32(&bars->v_empty[s]), ph ^ 1, abort, p.status,
+                       kStatusTimeoutProducer))
+          break;
+        mbar_arrive_expect_tx(smem_u32(&bars->v_full[s]), kTileBytes);
+        tma_load_5d(sV + s * kTileBytes, &tmap_v, smem_u32(&bars->v_full[s]), 0, l0, head, batch,
+                    seg);
+      }
+      if (*abort) {
+        // Let every load this thread may have started land before the CTA
+        // exits (on the normal path the consumers have already seen them).
+        mbar_wait_drain(qbar, 0);
+        for (int j = (n_kv > kStages ? n_kv - kStages : 0); j < n_kv; ++j) {
+          const int s = j % kStages;
+          const uint32_t ph = (j / kStages) & 1;
+          mbar_wait_drain(smem_u32(&bars->k_full[s]), ph);
+          mbar_wait_drain(smem_u32(&bars->v_full[s]), ph);
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_bf16_f32(kBlockM, kBlockN, false, false);
+      constexpr uint32_t idesc_pv = idesc_bf16_f32(kBlockM, kHeadDim, false, true);
+      const uint32_t tS[2] = {tmem + 0, tmem + 128};
+      const uint32_t tO[2] = {tmem + 256, tmem + 320};
+      const uint32_t tP[2] = {tmem + 384, tmem + 448};
+      auto issue_qk = [&](int t, int s) {
+        const uint32_t qa = sQ + t * kTileBytes;
+        const uint32_t ka = sK + s * kTileBytes;
+#pragma unroll
+        for (int k = 0; k < kHeadDim / 16; ++k) {
+          mma_bf16_ss(tS[t], sdesc_sw128(qa + k * 32, 16, 1024), sdesc_sw128(ka + k * 32, 16, 1024),
+                      idesc_qk, k > 0);
+        }
+      };
+      auto issue_pv = [&](int t, int s, bool accumulate) {
+        const uint32_t va = sV + s * kTileBytes;
+#pragma unroll
+        for (int k = 0; k < kBlockN / 16; ++k) {
+          mma_bf16_ts(tO[t], tP[t] + k * 8, sdesc_sw128(va + k * 2048, 1024, 1024), idesc_pv,
+                      (accumulate || k > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(smem_u32(&bars->q_full), 0, abort, p.status, kStatusTimeoutMma) &&
+                mbar_wait(smem_u32(&bars->k_full[0]), 0, abort, p.status, kStatusTimeoutMma);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0, 0);
+        mma_commit(smem_u32(&bars->s_full[0]));
+        issue_qk(1, 0);
+        mma_commit(smem_u32(&bars->s_full[1]));
+        mma_commit(smem_u32(&bars->k_empty[0]));
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j % kStages;
+        const uint32_t ph = (j / kStages) & 1;
+        const int s1 = (j + 1) % kStages;
+        const uint32_t ph1 = ((j + 1) / kStages) & 1;
+        const bool more = j + 1 < n_kv;
+        // query tile A
+        if (!mbar_wait(smem_u32(&bars->p_full[0]), j & 1, abort, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+        if (more) {
+          if (!mbar_wait(smem_u32(&bars->k_full[s1]), ph1, abort, p.status, kStatusTimeoutMma))
+            break;
+          tc_fence_after();
+          issue_qk(0, s1);
+          mma_commit(smem_u32(&bars->s_full[0]));
+        }
+        if (!mbar_wait(smem_u32(&bars->v_full[s]), ph, abort, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+        issue_pv(0, s, j > 0);
+        mma_commit(smem_u32(&bars->o_done[0]));
+        // query tile B
+        if (!mbar_wait(smem_u32(&bars->p_full[1]), j & 1, abort, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+        if (more) {
+          issue_qk(1, s1);
+          mma_commit(smem_u32(&bars->s_full[1]));
+          mma_commit(smem_u32(&bars->k_empty[s1]));
+        }
+        issue_pv(1, s, j > 0);
+        mma_commit(smem_u32(&bars->o_done[1]));
+        mma_commit(smem_u32(&bars->v_empty[s]));
+      }
+      // Every MMA this thread issued completes before TMEM is released.
+      mma_commit(smem_u32(&bars->mma_drain));
+      mbar_wait_drain(smem_u32(&bars->mma_drain), 0);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int t = warp >> 2;             // query tile of this warpgroup
+    const int row = threadIdx.x & 127;   // query row within the tile == TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + t * 128 + lane_off;
+    const uint32_t tO = tmem + 256 + t * 64 + lane_off;
+    const uint32_t tP = tmem + 384 + t * 64 + lane_off;
+    const float c = p.scale_log2;
+    float m_run = -CUDART_INF_F;  // running max of S * c (log2 domain)
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      // Wait results are made warp-uniform: tcgen05.ld/st are .sync.aligned.
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->s_full[t]), j & 1, abort, p.status,
+                                             kStatusTimeoutSoftmax))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      int seg, l0;
+      tile_coords(j, p.tiles_per_seg, seg, l0);
+      const int valid = min(kBlockN, p.seg_len - l0);
+      // Pass 1: row max over the whole S row (registers released afterwards).
+      float mx0 = -CUDART_INF_F, mx1 = -CUDART_INF_F, mx2 = -CUDART_INF_F, mx3 = -CUDART_INF_F;
+      {
+        uint32_t sr[128];
+        tmem_ld_wait_128(tS, sr);
+        if (valid < kBlockN) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i >= valid) sr[i] = __float_as_uint(-CUDART_INF_F);
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          mx0 = fmaxf(mx0, __uint_as_float(sr[i]));
+          mx1 = fmaxf(mx1, __uint_as_float(sr[32 + i]));
+          mx2 = fmaxf(mx2, __uint_as_float(sr[64 + i]));
+          mx3 = fmaxf(mx3, __uint_as_float(sr[96 + i]));
+        }
+      }
+      const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;
+      float m_new = m_run;
+      bool rescale = false;
+      if (m_tile > m_run + kRescaleThreshold) {
+        m_new = m_tile;
+        rescale = j > 0;
+      }
+      if (j > 0) {
+        // P_t and O_t are free once the previous P V product has completed.
+        if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_done[t]), (j - 1) & 1, abort,
+                                               p.status, kStatusTimeoutSoftmax))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      // The O row update is done by the whole warp when any of its rows needs
+      // it (rows that do not need it scale by 1).
+      if (__any_sync(0xffffffffu, rescale)) {
+        const float alpha = rescale ? ex2_approx(m_run - m_new) : 1.0f;
+        l_run *= alpha;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t o[32];
+          tmem_ld_wait_32(tO + h * 32, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + h * 32, o);
+        }
+      }
+      m_run = m_new;
+      const float neg_m = -m_new;
+      float sum0 = 0.f, sum1 = 0.f;
+      // Pass 2: P = 2^(S c - m) in BF16, written to TMEM 64 S columns at a time.
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint32_t sr[64];
+        tmem_ld_wait_64(tS + h * 64, sr);
+        if (valid < kBlockN) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (h * 64 + i >= valid) sr[i] = __float_as_uint(-CUDART_INF_F);
+        }
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), c, neg_m));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), c, neg_m));
+          sum0 += p0;
+          sum1 += p1;
+          pk[i] = pack_bf16x2(p0, p1);
+        }
+        tmem_st32(tP + h * 32, pk);
+      }
+      l_run += sum0 + sum1;
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&bars->p_full[t]));
+    }
+    // ------------------------------------------------------------ epilogue
+    if (ok && __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_done[t]), (n_kv - 1) & 1, abort,
+                                                p.status, kStatusTimeoutEpilogue))) {
+      tc_fence_after();
+      uint32_t oflat[64];
+      tmem_ld_wait_64(tO, oflat);
+      uint32_t(&o)[2][32] = *reinterpret_cast<uint32_t(*)[2][32]>(oflat);
+      const int qt = 2 * pair + t;
+      if (qt < p.q_tiles) {
+        int seg, l0;
+        tile_coords(qt, p.tiles_per_seg, seg, l0);
+        const int tok = l0 + row;
+        if (tok < p.seg_len) {
+          const float inv_l = 1.0f / l_run;
+          __nv_bfloat16* dst = p.out + seg * p.o_ss + batch * p.o_bs + head * p.o_hs + tok * p.o_rs;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(o[h][8 * v + 0]) * inv_l,
+                                __uint_as_float(o[h][8 * v + 1]) * inv_l);
+              w.y = pack_bf16x2(__uint_as_float(o[h][8 * v + 2]) * inv_l,
+                                __uint_as_float(o[h][8 * v + 3]) * inv_l);
+              w.z = pack_bf16x2(__uint_as_float(o[h][8 * v + 4]) * inv_l,
+                                __uint_as_float(o[h][8 * v + 5]) * inv_l);
+              w.w = pack_bf16x2(__uint_as_float(o[h][8 * v + 6]) * inv_l,
+                                __uint_as_float(o[h][8 * v + 7]) * inv_l);
+              *reinterpret_cast<uint4*>(dst + h * 32 + v * 8) = w;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 8) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace erd
+
+using namespace erd;
+
+namespace {
+
+// Rank-5 tensor map {d, token, head, batch, segment} over a BF16 operand with
+// a 64 x 128 box and the 128-byte swizzle the MMA descriptors expect.
+int make_operand_map(CUtensorMap* map, const void* base, int seg_len, int heads, int batch,
+                     int nseg, int64_t ts, int64_t hs, int64_t bs, int64_t ss) {
+  const uint64_t dims[5] = {static_cast<uint64_t>(kHeadDim), static_cast<uint64_t>(seg_len),
+                            static_cast<uint64_t>(heads), static_cast<uint64_t>(batch),
+                            static_cast<uint64_t>(nseg)};
+  // Unused (size-1) dimensions still need a valid 16-byte-multiple stride.
+  auto stride = [](int64_t s, uint64_t n) -> uint64_t {
+    return n > 1 ? static_cast<uint64_t>(s) * 2 : 16;
+  };
+  const uint64_t strides[4] = {stride(ts, dims[1]), stride(hs, dims[2]), stride(bs, dims[3]),
+                               stride(ss, dims[4])};
+  const uint32_t box[5] = {kHeadDim, kBlockN, 1, 1, 1};
+  return encode_tensor_map(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(base), dims,
+                           strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+bool strides_ok(int64_t a, int64_t b, int64_t c, int64_t d) {
+  return a >= 0 && b >= 0 && c >= 0 && d >= 0 && ((a | b | c | d) & 7) == 0;
+}
+
+}  // namespace
+
+extern "C" int erd_attn_fwd_bf16(const void* q, const void* k, const void* v,
+                                 int64_t q_token_stride, int64_t q_head_stride,
+                                 int64_t q_batch_stride, int64_t q_seg_stride,
+                                 int64_t k_token_stride, int64_t k_head_stride,
+                                 int64_t k_batch_stride, int64_t k_seg_stride,
+                                 int64_t v_token_stride, int64_t v_head_stride,
+                                 int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads,
+                                 int seg_len, int nseg, int head_dim, float softmax_scale,
+                                 void* out, int64_t o_token_stride, int64_t o_head_stride,
+                                 int64_t o_batch_stride, int64_t o_seg_stride, int* status,
+                                 void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr) return kErrNullPointer;
+  if (head_dim != kHeadDim || batch <= 0 || heads <= 0 || seg_len <= 0 || nseg <= 0 ||
+      batch > 65535 || heads > 65535)
+    return kErrBadShape;
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return kErrMisaligned;
+  if (!strides_ok(q_token_stride, q_head_stride, q_batch_stride, q_seg_stride) ||
+      !strides_ok(k_token_stride, k_head_stride, k_batch_stride, k_seg_stride) ||
+      !strides_ok(v_token_stride, v_head_stride, v_batch_stride, v_seg_stride) ||
+      !strides_ok(o_token_stride, o_head_stride, o_batch_stride, o_seg_stride))
+    return kErrMisaligned;
+  if (int rc = check_device_sm100()) return rc;
+
+  const int tiles_per_seg = (seg_len + kBlockN - 1) / kBlockN;
+  const long long q_tiles = static_cast<long long>(tiles_per_seg) * nseg;
+  if (q_tiles > (1LL << 30)) return kErrTooLarge;
+
+  CUtensorMap tq, tk, tv;
+  if (make_operand_map(&tq, q, seg_len, heads, batch, nseg, q_token_stride, q_head_stride,
+                       q_batch_stride, q_seg_stride) ||
+      make_operand_map(&tk, k, seg_len, heads, batch, nseg, k_token_stride, k_head_stride,
+                       k_batch_stride, k_seg_stride) ||
+      make_operand_map(&tv, v, seg_len, heads, batch, nseg, v_token_stride, v_head_stride,
+                       v_batch_stride, v_seg_stride))
+    return kErrTensorMap;
+
+  AttnParams p;
+  p.seg_len = seg_len;
+  p.nseg = nseg;
+  p.tiles_per_seg = tiles_per_seg;
+  p.q_tiles = static_cast<int>(q_tiles);
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.o_rs = o_token_stride;
+  p.o_hs = o_head_stride;
+  p.o_bs = o_batch_stride;
+  p.o_ss = o_seg_stride;
+  p.status = status;
+
+  cudaError_t e = cudaFuncSetAttribute(attn_fwd_bf16_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kSmemLaunchBytes);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const dim3 grid(static_cast<unsigned>((q_tiles + 1) / 2), static_cast<unsigned>(heads),
+                  static_cast<unsigned>(batch));
+  attn_fwd_bf16_kernel<<<grid, kThreads, kSmemLaunchBytes, static_cast<cudaStream_t>(stream)>>>(
+      tq, tk, tv, p);
+  return static_cast<int>(cudaGetLastError());
+}

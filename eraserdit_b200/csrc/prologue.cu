@@ -1,0 +1,354 @@
+// Fused QK RMSNorm-across-heads + LTX 3D RoPE prologue, plus the per-axis
+// RoPE table builder.
+//
+// One warp per token.  Lane i owns the eight 16-byte chunks
+// c = 256 * it + 8 * i (it = 0..7) of the 2048-wide Q and K rows, so every
+// warp-wide load / store instruction moves 512 contiguous bytes.  Rounding
+// follows the unfused reference exactly: fp32 sum of squares, r = rsqrt(mean
+// + eps), y = bf16(x * r), z = bf16(y * w), out = bf16(z * cos + rot(z) * sin)
+// with separately rounded products (no FMA contraction), as in
+// models/dits/eraserdit_attention.py:68-79 and
+// layers/operator_fusion/triton/rmsnorm_native.py:25-43.  Only the order of
+// the fp32 sum of squares differs from torch's reduction.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "../../include/eraserdit_b200.h"
+#include "host_common.h"
+
+namespace erd {
+
+constexpr int kHidden = 2048;
+constexpr int kHeadDimP = 64;
+constexpr int kChunksPerLane = kHidden / 256;  // 8 chunks of 8 elements
+constexpr int kTokensPerBlock = 4;
+
+struct PrologueParams {
+  const __nv_bfloat16* q_in;
+  const __nv_bfloat16* k_in;
+  const __nv_bfloat16* v_in;
+  long long in_ts, in_bs;
+  int batch, tokens;
+  const __nv_bfloat16* wq;
+  const __nv_bfloat16* wk;
+  float eps;
+  const float* cos_tab;
+  const float* sin_tab;
+  long long tab_ts, tab_bs;
+  const float2* axis_tab;
+  int nfreq, grid_f, grid_h, grid_w, token_offset;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_out;
+  __nv_bfloat16* v_out;
+  long long out_ts, out_bs, out_hs, out_ds;
+  int heads_per_dest;
+};
+
+__device__ __forceinline__ float bf16_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+__device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i]));
+    const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i + 1]));
+    w[i] = lo | (hi << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// y = bf16(x * r), then z = bf16(y * w) when an affine weight is present.
+__device__ __forceinline__ void norm8(float (&x)[8], float r, const __nv_bfloat16* w, int c0) {
+  float wf[8];
+  if (w != nullptr) {
+    unpack8(__ldg(reinterpret_cast<const uint4*>(w + c0)), wf);
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    float y = bf16_round(__fmul_rn(x[e], r));
+    if (w != nullptr) y = bf16_round(__fmul_rn(y, wf[e]));
+    x[e] = y;
+  }
+}
+
+// out[2i] = z[2i] cos[2i] - z[2i+1] sin[2i]; out[2i+1] = z[2i+1] cos[2i+1] + z[2i] sin[2i+1]
+__device__ __forceinline__ void rope8(float (&z)[8], const float (&cs)[8], const float (&sn)[8]) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float a = z[2 * i], b = z[2 * i + 1];
+    z[2 * i] = __fadd_rn(__fmul_rn(a, cs[2 * i]), __fmul_rn(-b, sn[2 * i]));
+    z[2 * i + 1] = __fadd_rn(__fmul_rn(b, cs[2 * i + 1]), __fmul_rn(a, sn[2 * i + 1]));
+  }
+}
+
+template <int kRopeMode>
+__global__ void __launch_bounds__(kTokensPerBlock * 32, 3)
+    qk_norm_rope_kernel(const PrologueParams p) {
+  const int lane = threadIdx.x & 31;
+  const long long g = static_cast<long long>(blockIdx.x) * kTokensPerBlock + (threadIdx.x >> 5);
+  if (g >= static_cast<long long>(p.batch) * p.tokens) return;
+  const int b = static_cast<int>(g / p.tokens);
+  const int t = static_cast<int>(g - static_cast<long long>(b) * p.tokens);
+
+  // V is only repacked: copy it first so that its registers are free again
+  // before Q and K are loaded.
+  if (p.v_in != nullptr && p.v_out != nullptr) {
+    const __nv_bfloat16* vrow = p.v_in + b * p.in_bs + t * p.in_ts;
+    uint4 vv[kChunksPerLane];
+#pragma unroll
+    for (int it = 0; it < kChunksPerLane; ++it)
+      vv[it] = *reinterpret_cast<const uint4*>(vrow + it * 256 + lane * 8);
+#pragma unroll
+    for (int it = 0; it < kChunksPerLane; ++it) {
+      const int c0 = it * 256 + lane * 8;
+      const int head = c0 / kHeadDimP;
+      const int dest = head / p.heads_per_dest;
+      const int hl = head - dest * p.heads_per_dest;
+      *reinterpret_cast<uint4*>(p.v_out + b * p.out_bs + t * p.out_ts + hl * p.out_hs +
+                                dest * p.out_ds + (c0 - head * kHeadDimP)) = vv[it];
+    }
+  }
+
+  const __nv_bfloat16* qrow = p.q_in + b * p.in_bs + t * p.in_ts;
+  const __nv_bfloat16* krow = p.k_in + b * p.in_bs + t * p.in_ts;
+  uint4 qv[kChunksPerLane], kv[kChunksPerLane];
+#pragma unroll
+  for (int it = 0; it < kChunksPerLane; ++it) {
+    const int c0 = it * 256 + lane * 8;
+    qv[it] = *reinterpret_cast<const uint4*>(qrow + c0);
+    kv[it] = *reinterpret_cast<const uint4*>(krow + c0);
+  }
+
+  // fp32 sum of squares over the full 2048-wide rows (squares of BF16 values
+  // are exact in fp32).
+  float sq = 0.f, sk = 0.f;
+#pragma unroll
+  for (int it = 0; it < kChunksPerLane; ++it) {
+    float f[8];
+    unpack8(qv[it], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sq = __fadd_rn(sq, __fmul_rn(f[e], f[e]));
+    unpack8(kv[it], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sk = __fadd_rn(sk, __fmul_rn(f[e], f[e]));
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    sq += __shfl_xor_sync(0xffffffffu, sq, off);
+    sk += __shfl_xor_sync(0xffffffffu, sk, off);
+  }
+  // 1 / sqrt with IEEE rounding of both steps, as torch's CPU rsqrt computes it.
+  const float rq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(sq * (1.0f / kHidden), p.eps)));
+  const float rk = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(sk * (1.0f / kHidden), p.eps)));
+
+  int pos_f = 0, pos_h = 0, pos_w = 0;
+  if (kRopeMode == 2) {
+    const int gpos = p.token_offset + t;
+    const int hw = p.grid_h * p.grid_w;
+    pos_f = gpos / hw;
+    const int rem = gpos - pos_f * hw;
+    pos_h = rem / p.grid_w;
+    pos_w = rem - pos_h * p.grid_w;
+  }
+
+#pragma unroll
+  for (int it = 0; it < kChunksPerLane; ++it) {
+    const int c0 = it * 256 + lane * 8;
+    float q[8], k[8];
+    unpack8(qv[it], q);
+    unpack8(kv[it], k);
+    norm8(q, rq, p.wq, c0);
+    norm8(k, rk, p.wk, c0);
+    if (kRopeMode != 0) {
+      float cs[8], sn[8];
+      if (kRopeMode == 1) {
+        const float* cb = p.cos_tab + b * p.tab_bs + t * p.tab_ts + c0;
+        const float* sb = p.sin_tab + b * p.tab_bs + t * p.tab_ts + c0;
+        const float4 c_lo = __ldg(reinterpret_cast<const float4*>(cb));
+        const float4 c_hi = __ldg(reinterpret_cast<const float4*>(cb + 4));
+        const float4 s_lo = __ldg(reinterpret_cast<const float4*>(sb));
+        const float4 s_hi = __ldg(reinterpret_cast<const float4*>(sb + 4));
+        cs[0] = c_lo.x; cs[1] = c_lo.y; cs[2] = c_lo.z; cs[3] = c_lo.w;
+        cs[4] = c_hi.x; cs[5] = c_hi.y; cs[6] = c_hi.z; cs[7] = c_hi.w;
+        sn[0] = s_lo.x; sn[1] = s_lo.y; sn[2] = s_lo.z; sn[3] = s_lo.w;
+        sn[4] = s_hi.x; sn[5] = s_hi.y; sn[6] = s_hi.z; sn[7] = s_hi.w;
+      } else {
+        // Channel pair (c, c+1), c even: c < 2 -> identity; otherwise pair
+        // index p = (c - 2) / 2 uses frequency p / 3 on axis p % 3
+        // (eraserdit_transformer.py:202-212).
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = c0 + 2 * i;
+          float cv = 1.f, sv = 0.f;
+          if (c >= 2) {
+            const int pr = (c - 2) >> 1;
+            const int kf = pr / 3;
+            const int axis = pr - 3 * kf;
+            int base, coord;
+            if (axis == 0) {
+              base = 0;
+              coord = pos_f;
+            } else if (axis == 1) {
+              base = p.grid_f * p.nfreq;
+              coord = pos_h;
+            } else {
+              base = (p.grid_f + p.grid_h) * p.nfreq;
+              coord = pos_w;
+            }
+            const float2 e = __ldg(p.axis_tab + base + coord * p.nfreq + kf);
+            cv = e.x;
+            sv = e.y;
+          }
+          cs[2 * i] = cv;
+          cs[2 * i + 1] = cv;
+          sn[2 * i] = sv;
+          sn[2 * i + 1] = sv;
+        }
+      }
+      rope8(q, cs, sn);
+      rope8(k, cs, sn);
+    }
+    const int head = c0 / kHeadDimP;
+    const int d0 = c0 - head * kHeadDimP;
+    const int dest = head / p.heads_per_dest;
+    const int hl = head - dest * p.heads_per_dest;
+    const long long off = b * p.out_bs + t * p.out_ts + hl * p.out_hs + dest * p.out_ds + d0;
+    *reinterpret_cast<uint4*>(p.q_out + off) = pack8(q);
+    *reinterpret_cast<uint4*>(p.k_out + off) = pack8(k);
+  }
+}
+
+// One thread per (axis, coordinate, frequency) entry.
+__global__ void rope_axis_table_kernel(const float* __restrict__ freqs, int nfreq, int frames,
+                                       int height, int width, int use_scale, float scale_f,
+                                       float scale_h, float scale_w, float patch_t, float patch_s,
+                                       float base_f, float base_h, float base_w,
+                                       float2* __restrict__ table) {
+  const int total = (frames + height + width) * nfreq;
+  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int kf = idx % nfreq;
+  const int i_all = idx / nfreq;
+  float coord;
+  if (i_all < frames) {
+    coord = static_cast<float>(i_all);
+    if (use_scale) coord = __fdiv_rn(__fmul_rn(__fmul_rn(coord, scale_f), patch_t), base_f);
+  } else if (i_all < frames + height) {
+    coord = static_cast<float>(i_all - frames);
+    if (use_scale) coord = __fdiv_rn(__fmul_rn(__fmul_rn(coord, scale_h), patch_s), base_h);
+  } else {
+    coord = static_cast<float>(i_all - frames - height);
+    if (use_scale) coord = __fdiv_rn(__fmul_rn(__fmul_rn(coord, scale_w), patch_s), base_w);
+  }
+  const float angle = __fmul_rn(freqs[kf], __fadd_rn(__fmul_rn(coord, 2.0f), -1.0f));
+  float s, c;
+  sincosf(angle, &s, &c);
+  table[idx] = make_float2(c, s);
+}
+
+}  // namespace erd
+
+using namespace erd;
+
+extern "C" int erd_rope_axis_table(const float* freqs, int nfreq, int frames, int height, int width,
+                                   int use_scale, float scale_f, float scale_h, float scale_w,
+                                   float patch_t, float patch_s, float base_f, float base_h,
+                                   float base_w, float* table, void* stream) {
+  if (freqs == nullptr || table == nullptr) return kErrNullPointer;
+  if (nfreq <= 0 || frames <= 0 || height <= 0 || width <= 0) return kErrBadShape;
+  if (int rc = check_device_sm100()) return rc;
+  const int total = (frames + height + width) * nfreq;
+  rope_axis_table_kernel<<<(total + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      freqs, nfreq, frames, height, width, use_scale, scale_f, scale_h, scale_w, patch_t, patch_s,
+      base_f, base_h, base_w, reinterpret_cast<float2*>(table));
+  return static_cast<int>(cudaGetLastError());
+}
+
+extern "C" int erd_qk_norm_rope(const void* q_in, const void* k_in, const void* v_in,
+                                int64_t in_token_stride, int64_t in_batch_stride, int batch,
+                                int tokens, int hidden, const void* q_weight, const void* k_weight,
+                                float eps, int rope_mode, const float* cos_tab,
+                                const float* sin_tab, int64_t tab_token_stride,
+                                int64_t tab_batch_stride, const float* axis_table, int nfreq,
+                                int frames, int height, int width, int token_offset, void* q_out,
+                                void* k_out, void* v_out, int64_t out_token_stride,
+                                int64_t out_batch_stride, int64_t out_head_stride,
+                                int heads_per_dest, int64_t out_dest_stride, void* stream) {
+  if (q_in == nullptr || k_in == nullptr || q_out == nullptr || k_out == nullptr)
+    return kErrNullPointer;
+  if (hidden != kHidden || batch < 0 || tokens < 0 || heads_per_dest <= 0 ||
+      (kHidden / kHeadDimP) % heads_per_dest != 0)
+    return kErrBadShape;
+  if (rope_mode < 0 || rope_mode > 2) return kErrBadShape;
+  if (rope_mode == 1 && (cos_tab == nullptr || sin_tab == nullptr)) return kErrNullPointer;
+  if (rope_mode == 2) {
+    if (axis_table == nullptr) return kErrNullPointer;
+    if (nfreq != kHidden / 6 || frames <= 0 || height <= 0 || width <= 0 || token_offset < 0 ||
+        static_cast<long long>(token_offset) + tokens >
+            static_cast<long long>(frames) * height * width)
+      return kErrBadShape;
+  }
+  const void* ptrs[] = {q_in, k_in, q_out, k_out, q_weight, k_weight, v_in, v_out};
+  for (const void* ptr : ptrs)
+    if (ptr != nullptr && !aligned16(ptr)) return kErrMisaligned;
+  if ((in_token_stride | in_batch_stride | out_token_stride | out_batch_stride | out_head_stride |
+       out_dest_stride) & 7)
+    return kErrMisaligned;
+  if (rope_mode == 1 && (!aligned16(cos_tab) || !aligned16(sin_tab) ||
+                         ((tab_token_stride | tab_batch_stride) & 3)))
+    return kErrMisaligned;
+  if (int rc = check_device_sm100()) return rc;
+  if (batch == 0 || tokens == 0) return kErrOk;
+
+  PrologueParams p;
+  p.q_in = static_cast<const __nv_bfloat16*>(q_in);
+  p.k_in = static_cast<const __nv_bfloat16*>(k_in);
+  p.v_in = static_cast<const __nv_bfloat16*>(v_in);
+  p.in_ts = in_token_stride;
+  p.in_bs = in_batch_stride;
+  p.batch = batch;
+  p.tokens = tokens;
+  p.wq = static_cast<const __nv_bfloat16*>(q_weight);
+  p.wk = static_cast<const __nv_bfloat16*>(k_weight);
+  p.eps = eps;
+  p.cos_tab = cos_tab;
+  p.sin_tab = sin_tab;
+  p.tab_ts = tab_token_stride;
+  p.tab_bs = tab_batch_stride;
+  p.axis_tab = reinterpret_cast<const float2*>(axis_table);
+  p.nfreq = nfreq;
+  p.grid_f = frames;
+  p.grid_h = height;
+  p.grid_w = width;
+  p.token_offset = token_offset;
+  p.q_out = static_cast<__nv_bfloat16*>(q_out);
+  p.k_out = static_cast<__nv_bfloat16*>(k_out);
+  p.v_out = static_cast<__nv_bfloat16*>(v_out);
+  p.out_ts = out_token_stride;
+  p.out_bs = out_batch_stride;
+  p.out_hs = out_head_stride;
+  p.out_ds = out_dest_stride;
+  p.heads_per_dest = heads_per_dest;
+
+  const long long rows = static_cast<long long>(batch) * tokens;
+  const unsigned grid = static_cast<unsigned>((rows + kTokensPerBlock - 1) / kTokensPerBlock);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (rope_mode) {
+    case 0: qk_norm_rope_kernel<0><<<grid, kTokensPerBlock * 32, 0, s>>>(p); break;
+    case 1: qk_norm_rope_kernel<1><<<grid, kTokensPerBlock * 32, 0, s>>>(p); break;
+    default: qk_norm_rope_kernel<2><<<grid, kTokensPerBlock * 32, 0, s>>>(p); break;
+  }
+  return static_cast<int>(cudaGetLastError());
+}

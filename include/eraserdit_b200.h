@@ -1,0 +1,112 @@
+/*
+ * eraserdit_b200 -- C ABI of the B200 (sm_100a) DiT self-attention hot path.
+ *
+ * Conventions (the style of the reference's mask-STA ctypes library,
+ * layers/attention/backends/mask_sta.py:108-131 and
+ * layers/attention/backends/csrc/mask_sta/core.cu:767-788):
+ *   - every entry point takes raw device pointers, plain sizes, strides in
+ *     ELEMENTS (not bytes) and the caller's CUDA stream (as void*);
+ *   - the caller owns every buffer; nothing here allocates device memory;
+ *   - work is only enqueued on the given stream; no host synchronisation;
+ *   - the return value is 0 on success, a positive cudaError_t from the
+ *     launch, or a negative argument error detected before launching
+ *     (erd_error_string() describes it);
+ *   - `status` pointers (may be NULL) receive device-side error bits: a wait
+ *     inside a kernel that timed out (the kernel then returns early instead of
+ *     hanging).  The caller reads them after synchronising.
+ * BF16 tensors are passed as void* (16-bit words).
+ */
+#ifndef ERASERDIT_B200_H_
+#define ERASERDIT_B200_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ERD_ABI_VERSION 1
+
+/* ABI version probe; replaces eraserdit_mask_sta_abi()
+ * (layers/attention/backends/csrc/mask_sta/core.cu:767). */
+int erd_abi_version(void);
+
+/* Human-readable text for a return code of any entry point. */
+const char* erd_error_string(int code);
+
+/*
+ * Per-axis RoPE table for the LTX 3D rotary embedding.
+ * Replaces the table built by LTXVideoRotaryPosEmbed.forward
+ * (models/dits/eraserdit_transformer.py:136-214) in factored form: for axis a
+ * in (frame, height, width), coordinate i and frequency k it stores
+ * (cos, sin)(freqs[k] * (2 * coord_a(i) - 1)) as float2 at
+ * table[2 * (axis_base(a) + i * nfreq + k)], axis_base = 0, F*nfreq,
+ * (F+H)*nfreq.  coord_a(i) = i, or, when use_scale != 0,
+ * i * scale_a * patch_a / base_a evaluated left to right in fp32 (:153-156).
+ * `freqs` are the nfreq = dim/6 base frequencies of :194-201 (device, fp32).
+ */
+int erd_rope_axis_table(const float* freqs, int nfreq, int frames, int height, int width,
+                        int use_scale, float scale_f, float scale_h, float scale_w,
+                        float patch_t, float patch_s, float base_f, float base_h, float base_w,
+                        float* table, void* stream);
+
+/*
+ * Fused QK RMSNorm across heads + 3D RoPE, optionally copying V, writing Q/K/V
+ * straight into a head-major destination layout.
+ * Replaces apply_fused_qk_rmsnorm_rope
+ * (layers/operator_fusion/qk_rmsnorm_rope.py:80-152; semantics of the unfused
+ * closure models/dits/eraserdit_attention.py:259-281 with diffusers RMSNorm,
+ * rounding boundaries as layers/operator_fusion/triton/rmsnorm_native.py:25-43)
+ * and the Ulysses send packing (layers/attention/qkv_packing.py:31-48,
+ * models/adapters/eraserdit/nccl_sequence.py:56-65).
+ *
+ * Inputs: q_in/k_in (and v_in, may be NULL) BF16 [batch][tokens][hidden] with
+ * the given token / batch strides; hidden must be 2048 (32 heads x 64).
+ * q_weight/k_weight: BF16 [hidden] RMSNorm weights or NULL (no affine).
+ * rope_mode 0: no RoPE; 1: full fp32 cos/sin tables indexed
+ * [b * tab_batch_stride + t * tab_token_stride + c]; 2: per-axis table from
+ * erd_rope_axis_table, token t of this call sitting at grid position
+ * token_offset + t of a frames x height x width grid.
+ * Outputs: element (b, t, head h, d) goes to
+ *   out + b*out_batch_stride + t*out_token_stride
+ *       + (h % heads_per_dest)*out_head_stride + (h / heads_per_dest)*out_dest_stride + d.
+ * Outputs may alias the inputs exactly (in place).
+ */
+int erd_qk_norm_rope(const void* q_in, const void* k_in, const void* v_in,
+                     int64_t in_token_stride, int64_t in_batch_stride, int batch, int tokens,
+                     int hidden, const void* q_weight, const void* k_weight, float eps,
+                     int rope_mode, const float* cos_tab, const float* sin_tab,
+                     int64_t tab_token_stride, int64_t tab_batch_stride, const float* axis_table,
+                     int nfreq, int frames, int height, int width, int token_offset, void* q_out,
+                     void* k_out, void* v_out, int64_t out_token_stride, int64_t out_batch_stride,
+                     int64_t out_head_stride, int heads_per_dest, int64_t out_dest_stride,
+                     void* stream);
+
+/*
+ * Non-causal, unmasked attention, head_dim 64, BF16 in/out, FP32 softmax and
+ * accumulation, on tcgen05 tensor cores with TMEM accumulators.
+ * Replaces SDPAImpl.forward (layers/attention/backends/sdpa.py:56-80) as
+ * called from models/dits/eraserdit_attention.py:287-289 and from the Ulysses
+ * path after the sequence-to-head exchange (nccl_sequence.py:259-260).
+ *
+ * The sequence of every (batch, head) is `nseg` segments of `seg_len` tokens
+ * (nseg = 1 for one GPU; one segment per source rank after the all-to-all).
+ * Element (b, h, segment s, token t, d) of X in {q, k, v} is at
+ *   X + s*x_seg_stride + b*x_batch_stride + h*x_head_stride + t*x_token_stride + d,
+ * and the output row goes to the same formula with the o_* strides.
+ * Pointers must be 16-byte aligned and strides multiples of 8 elements.
+ */
+int erd_attn_fwd_bf16(const void* q, const void* k, const void* v, int64_t q_token_stride,
+                      int64_t q_head_stride, int64_t q_batch_stride, int64_t q_seg_stride,
+                      int64_t k_token_stride, int64_t k_head_stride, int64_t k_batch_stride,
+                      int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+                      int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads,
+                      int seg_len, int nseg, int head_dim, float softmax_scale, void* out,
+                      int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride,
+                      int64_t o_seg_stride, int* status, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ERASERDIT_B200_H_ */
