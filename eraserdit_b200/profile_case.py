@@ -1,0 +1,55 @@
+"""Small, self-contained workloads for ncu captures of the path's kernels.
+
+    python -m eraserdit_b200.profile_case attention --batch 1 --seq 16320 --iters 3
+    python -m eraserdit_b200.profile_case prologue --batch 2 --seq 32640 --iters 3
+
+Each runs the named kernel ``iters`` times on seeded inputs (sized above L2 by
+default) and exits 0, so that an ncu capture (``-k``/``-c``) of one to three
+launches ends by itself.
+"""
+
+from __future__ import annotations
+
+import argparse
+
+import torch
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kernel", choices=["attention", "prologue"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--seq", type=int, default=16320)
+    ap.add_argument("--heads", type=int, default=32)
+    ap.add_argument("--iters", type=int, default=3)
+    args = ap.parse_args()
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device).manual_seed(0)
+    from eraserdit_b200 import _native
+    if args.kernel == "attention":
+        from eraserdit_b200.attention import attention_bshd
+        qkv = torch.randn(args.batch, args.seq, 3, args.heads, 64, generator=g,
+                          device=device).bfloat16()
+        out = torch.empty(args.batch, args.seq, args.heads, 64, device=device,
+                          dtype=torch.bfloat16)
+        for _ in range(args.iters):
+            attention_bshd(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], 0.125, out=out)
+    else:
+        from eraserdit_b200.operator_fusion import qk_norm_rope_into
+        from eraserdit_b200.rotary import LTXVideoRotaryPosEmbed
+        frames = max(1, args.seq // (34 * 60))
+        rope = LTXVideoRotaryPosEmbed()(frames, 34, 60, device=device)
+        seq = rope.tokens
+        qkv = torch.randn(args.batch, seq, 6144, generator=g, device=device).bfloat16()
+        w = torch.ones(2048, device=device, dtype=torch.bfloat16)
+        q, k = qkv[..., :2048], qkv[..., 2048:4096]
+        for _ in range(args.iters):
+            qk_norm_rope_into(q, k, w, w, 1e-6, rope, q, k)
+    torch.cuda.synchronize()
+    if _native.read_status(device):
+        raise SystemExit("a kernel wait timed out")
+
+
+if __name__ == "__main__":
+    main()

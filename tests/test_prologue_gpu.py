@@ -19,10 +19,22 @@ def _fusion():
     return apply_fused_qk_rmsnorm_rope
 
 
-def _assert_close_bf16(got, want, max_ulp=1, max_frac=1e-3):
-    d = bf16_ulp_distance(got.cpu(), want.cpu())
-    assert int(d.max()) <= max_ulp, f"max ulp {int(d.max())}"
+def _assert_close_bf16(got, want, max_frac=1e-3):
+    """Kernel and reference differ only in the order of the fp32 sum of squares.
+    That moves a normalised value by at most one BF16 ulp, rarely; after RoPE a
+    cancelling pair can turn that into several ulps of a near-zero result, so
+    the bound is absolute (one ulp of the row scale) plus a mismatch budget and
+    the reference's own rel-RMSE bar for fused QK norm/RoPE (< 1e-3,
+    tests/test_qk_fast_fusion.py:55-57 of the reference)."""
+    got, want = got.cpu(), want.cpu()
+    d = bf16_ulp_distance(got, want)
     assert float((d > 0).float().mean()) <= max_frac
+    diff = (got.float() - want.float()).abs()
+    row_scale = want.float().abs().amax(dim=-1, keepdim=True)
+    assert bool((diff <= row_scale * 2.0 ** -7).all()), float((diff / row_scale).max())
+    rel = ((got.float() - want.float()).square().mean()
+           / want.float().square().mean().clamp_min(1e-30)).sqrt()
+    assert float(rel) < 1e-3
 
 
 @pytest.mark.parametrize("tag", ["a", "b"])
