@@ -41,6 +41,13 @@ constexpr int kStages = 3;  // K and V ring depth
 constexpr int kTileBytes = kBlockM * kHeadDim * 2;  // 16 KB
 constexpr int kThreads = 320;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only if max grows > 2^8
+// Of every 8 consecutive column pairs of a P row, this many are exponentiated
+// with the FMA-pipe polynomial and the rest with MUFU ex2, balancing the two
+// pipes (MUFU alone is the softmax bottleneck at head_dim 64).
+#ifndef ERD_POLY_EVERY8
+#define ERD_POLY_EVERY8 2
+#endif
+constexpr int kPolyPairsPer8 = ERD_POLY_EVERY8;
 
 struct AttnParams {
   int seg_len;
@@ -276,11 +283,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (i >= valid) sr[i] = __float_as_uint(-CUDART_INF_F);
         }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          mx0 = fmaxf(mx0, __uint_as_float(sr[i]));
-          mx1 = fmaxf(mx1, __uint_as_float(sr[32 + i]));
-          mx2 = fmaxf(mx2, __uint_as_float(sr[64 + i]));
-          mx3 = fmaxf(mx3, __uint_as_float(sr[96 + i]));
+        for (int i = 0; i < 32; i += 2) {
+          mx0 = fmax3(mx0, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+          mx1 = fmax3(mx1, __uint_as_float(sr[32 + i]), __uint_as_float(sr[33 + i]));
+          mx2 = fmax3(mx2, __uint_as_float(sr[64 + i]), __uint_as_float(sr[65 + i]));
+          mx3 = fmax3(mx3, __uint_as_float(sr[96 + i]), __uint_as_float(sr[97 + i]));
         }
       }
       const float m_tile = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * c;
@@ -329,10 +336,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float p0 = ex2_approx(fmaf(__uint_as_float(sr[2 * i]), c, neg_m));
-          const float p1 = ex2_approx(fmaf(__uint_as_float(sr[2 * i + 1]), c, neg_m));
-          sum0 += p0;
-          sum1 += p1;
+          float x0, x1, p0, p1;
+          fma2(x0, x1, __uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1]), c, c, neg_m,
+               neg_m);
+          if ((i & 7) < kPolyPairsPer8) {
+            exp2_poly2(x0, x1, p0, p1);
+          } else {
+            p0 = ex2_approx(x0);
+            p1 = ex2_approx(x1);
+          }
+          add2(sum0, sum1, sum0, sum1, p0, p1);
           pk[i] = pack_bf16x2(p0, p1);
         }
         tmem_st32(tP + h * 32, pk);

@@ -197,6 +197,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -245,6 +255,66 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
+}
+
+// Packed FP32 pair arithmetic (sm_100 f32x2 instructions: two lanes of work
+// per issue slot).
+#define ERD_F32X2_OP(name, op)                                                              \
+  __device__ __forceinline__ void name(float& d0, float& d1, float a0, float a1, float b0,  \
+                                       float b1) {                                          \
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"                                                   \
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t" op                            \
+        " rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"                                        \
+        : "=f"(d0), "=f"(d1)                                                                \
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));                                              \
+  }
+ERD_F32X2_OP(add2, "add.rn.f32x2")
+ERD_F32X2_OP(add2_rm, "add.rm.f32x2")
+ERD_F32X2_OP(sub2, "sub.rn.f32x2")
+#undef ERD_F32X2_OP
+
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0, float b1,
+                                     float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d0), "=f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of x <= 0 on the FMA pipe (no MUFU): Cody-Waite split into
+// 2^floor(x) (added to the exponent field) times a cubic minimax fit of 2^f,
+// f in [0, 1), max relative error 7.5e-5 (coefficients from
+// gen_exp2_poly.py).  Inputs below -126 (masked columns) are clamped; their
+// result is ~1e-38, i.e. zero after the BF16 P rounding.  (The cubic's value
+// at f = 0 is just below 1, so its exponent field is 126; -126 is the lowest
+// shift that cannot wrap the exponent.)
+constexpr float kExp2C0 = 0x1.fff634p-1f;
+constexpr float kExp2C1 = 0x1.644450p-1f;
+constexpr float kExp2C2 = 0x1.cefc08p-3f;
+constexpr float kExp2C3 = 0x1.3f970ap-4f;
+constexpr float kRoundMagic = 0x1.8p23f;  // 1.5 * 2^23: adding it leaves floor(x) in the low bits
+
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
+  x0 = fmaxf(x0, -126.0f);
+  x1 = fmaxf(x1, -126.0f);
+  float t0, t1, j0, j1, f0, f1, p0, p1;
+  add2_rm(t0, t1, x0, x1, kRoundMagic, kRoundMagic);  // t = magic + floor(x)
+  sub2(j0, j1, t0, t1, kRoundMagic, kRoundMagic);     // floor(x), exact
+  sub2(f0, f1, x0, x1, j0, j1);                       // f in [0, 1), exact
+  fma2(p0, p1, kExp2C3, kExp2C3, f0, f1, kExp2C2, kExp2C2);
+  fma2(p0, p1, p0, p1, f0, f1, kExp2C1, kExp2C1);
+  fma2(p0, p1, p0, p1, f0, f1, kExp2C0, kExp2C0);
+  // floor(x) sits in the low mantissa bits of t; shifting by 23 moves it into
+  // the exponent field (the high bits of t shift out).
+  y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
 }  // namespace erd
