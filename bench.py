@@ -300,6 +300,7 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", default="native", choices=["native", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--cfg", type=int, default=1, help="CFG branches on separate rank groups")
     args = parser.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":

@@ -33,8 +33,9 @@ SIGNATURES = {
                          _c_float, _c_int, _vp, _vp, _c_i64, _c_i64, _vp, _c_int, _c_int, _c_int,
                          _c_int, _c_int, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_i64,
                          _vp],
-    "erd_attn_fwd_bf16": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 5 + [_c_float, _vp]
-                         + [_c_i64] * 4 + [_vp, _vp],
+    "erd_attn_fwd_bf16": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 4 + [_vp, _c_int, _c_float,
+                                                                            _vp] + [_c_i64] * 4
+                         + [_vp, _vp],
 }
 
 _lib = None

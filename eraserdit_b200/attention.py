@@ -207,7 +207,7 @@ def attention_bshd(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
         rc = lib.erd_attn_fwd_bf16(
             query.data_ptr(), key.data_ptr(), value.data_ptr(),
             qs[1], qs[2], qs[0], 0, ks[1], ks[2], ks[0], 0, vs[1], vs[2], vs[0], 0,
-            batch, heads, seq, 1, dim, float(softmax_scale),
+            batch, heads, seq, 1, None, dim, float(softmax_scale),
             out.data_ptr(), os_[1], os_[2], os_[0], 0,
             _native.status_word(device).data_ptr(), _native.stream_handle(device))
     _native.check(rc, "erd_attn_fwd_bf16")

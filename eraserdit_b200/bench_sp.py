@@ -1,5 +1,130 @@
-"""Multi-GPU (Ulysses SP) leg of bench.py."""
+"""Multi-GPU leg of ``bench.py``: Ulysses SP (optionally CFG x SP) over NCCL.
+
+Launched by torchrun with one process per GPU.  Every rank builds the same
+seeded layer and input, keeps its floor-partitioned tokens (CFG: its branch's
+batch entry) and runs the Ulysses layer; per-rank times come from CUDA events
+and the reported time is the maximum over ranks (an all-reduce MAX)."""
+
+from __future__ import annotations
+
+import json
+import os
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
 
 
-def run_sequence_parallel(args):
-    raise NotImplementedError("Ulysses SP bench leg is not built yet")
+def run_sequence_parallel(args) -> None:
+    import bench as B
+    from eraserdit_b200 import _native
+    from eraserdit_b200.topology import DiTGroups, DiTTopology
+    from eraserdit_b200.ulysses import UlyssesSelfAttention, peer_exchange
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch with torchrun")
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    try:
+        cfg = args.cfg
+        if world % cfg or B.BATCH % cfg:
+            raise SystemExit("CFG degree must divide the GPU count and the batch")
+        topo = DiTTopology(ulysses=world // cfg, cfg=cfg)
+        groups = DiTGroups(topo)
+        group, ranks, index = groups.get("ulysses") if world // cfg > 1 else (None, (rank,), 0)
+        cfg_index = topo.coordinates(rank)[3]
+        layer, rope = B.build_problem(device)
+        g = torch.Generator(device=device).manual_seed(1)
+        x_full = torch.randn(B.BATCH, B.SEQ, B.HIDDEN, generator=g, device=device).bfloat16()
+        per_branch = B.BATCH // cfg
+        x_branch = x_full[cfg_index * per_branch:(cfg_index + 1) * per_branch]
+        sp = UlyssesSelfAttention(layer, len(ranks), index, peer_exchange(group, ranks, index),
+                                  group_ranks=ranks)
+        x_local = x_branch[:, sp.partition(B.SEQ)].contiguous()
+        del x_full
+        stream = torch.cuda.current_stream(device)
+        attn_events = []
+
+        def step(record: bool):
+            s = sp.pre(x_local, rope, B.SEQ)
+            sp.exchange(*sp.send_recv_1(s))
+            if record:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+            sp.attend(s)
+            if record:
+                e1.record(stream)
+                attn_events.append((e0, e1))
+            sp.exchange(*sp.send_recv_2(s))
+            return sp.post(s)
+
+        for _ in range(args.warmup):
+            step(False)
+        torch.cuda.synchronize()
+        dist.barrier()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with B.ClockSampler(local) as clocks:
+            start.record(stream)
+            for _ in range(args.steps):
+                step(True)
+            stop.record(stream)
+            torch.cuda.synchronize()
+        dist.barrier()
+        ms = start.elapsed_time(stop) / args.steps
+        kernel_ms = sum(a.elapsed_time(b) for a, b in attn_events) / len(attn_events)
+        status = _native.read_status(device)
+
+        # End to end through the public API with host buffers (pinned).
+        host_x = x_local.cpu().pin_memory()
+        host_y = torch.empty_like(host_x).pin_memory()
+        for _ in range(max(args.warmup, 1)):
+            host_y.copy_(sp(host_x.to(device, non_blocking=True), rope, B.SEQ), non_blocking=True)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            host_y.copy_(sp(host_x.to(device, non_blocking=True), rope, B.SEQ), non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = e0.elapsed_time(e1) / args.steps
+
+        stats = torch.tensor([ms, kernel_ms, e2e_ms, float(status)], device=device)
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+        ms, kernel_ms, e2e_ms, status = stats.tolist()
+        clock = clocks.summary()
+        if rank == 0:
+            if status:
+                raise RuntimeError(f"kernel wait timed out on some rank (status {int(status)})")
+            peaks, src = B.measured_peaks()
+            peak_key = "bf16_tflops_sustained" if ms * args.steps >= 1000 else "bf16_tflops"
+            local_attn_flop = B.ATTN_FLOP / world
+            achieved = local_attn_flop / (kernel_ms / 1e3) / 1e12
+            parallelism = f"cfg{cfg}xsp{world // cfg}" if cfg > 1 else f"sp{world}"
+            print(json.dumps({
+                "metric": B.METRIC, "value": B.LAYER_FLOP / (ms / 1e3) / 1e12, "unit": B.UNIT,
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": B.WORKLOAD.replace("config 1", "config 2 (Ulysses SP)"),
+                           "global_batch": B.BATCH, "seq_len": B.SEQ, "parallelism": parallelism,
+                           "l2": "inputs larger than L2"},
+                "layer_tflop": B.LAYER_FLOP / 1e12,
+                "roofline": {"kernel": "attn_fwd_bf16 (per rank, max over ranks)",
+                             "bound": "tensor", "achieved": achieved, "peak": peaks[peak_key],
+                             "unit": B.UNIT, "frac": achieved / peaks[peak_key],
+                             "peak_source": f"{src} {peak_key}",
+                             "traffic": None, "kernel_ms": kernel_ms},
+                "e2e": {"value": B.LAYER_FLOP / (e2e_ms / 1e3) / 1e12, "unit": B.UNIT,
+                        "ms_per_step": e2e_ms,
+                        "h2d_bytes_per_step": host_x.numel() * host_x.element_size() * world,
+                        "d2h_bytes_per_step": host_y.numel() * host_y.element_size() * world},
+                "gpu_launches": 2 * args.steps,
+                "clocks": clock,
+            }), flush=True)
+    finally:
+        dist.destroy_process_group()

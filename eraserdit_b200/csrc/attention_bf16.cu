@@ -18,11 +18,12 @@
 // TMEM columns: S_A [0,128) S_B [128,256) O_A [256,320) O_B [320,384)
 //               P_A [384,448) P_B [448,512).
 //
-// The key / value sequence may be split into `nseg` segments of `seg_len`
-// tokens each (the layout the Ulysses all-to-all delivers: one segment per
-// source rank).  Tiles never straddle a segment; the last tile of a segment
-// is zero-filled by TMA and its missing columns are masked.  Queries use the
-// same tiling, and output rows are scattered back with the caller's strides.
+// The key / value sequence may be split into `nseg` segments held in slots of
+// `seg_len` tokens, segment s holding seg_lens[s] <= seg_len valid tokens
+// (the layout the Ulysses all-to-all delivers: one segment per source rank).
+// Tiles never straddle a segment; rows past a segment's end are masked (and
+// zero-filled by TMA past the slot).  Queries use the same tiling, and output
+// rows are scattered back with the caller's strides.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
@@ -49,7 +50,10 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only if max gr
 #endif
 constexpr int kPolyPairsPer8 = ERD_POLY_EVERY8;
 
+constexpr int kMaxSegments = 16;
+
 struct AttnParams {
+  int seg_lens[kMaxSegments];  // tokens of each segment (<= seg_len, the slot length)
   int seg_len;
   int nseg;
   int tiles_per_seg;
@@ -271,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       int seg, l0;
       tile_coords(j, p.tiles_per_seg, seg, l0);
-      const int valid = min(kBlockN, p.seg_len - l0);
+      const int valid = min(kBlockN, p.seg_lens[seg] - l0);
       // Pass 1: row max over the whole S row (registers released afterwards).
       float mx0 = -CUDART_INF_F, mx1 = -CUDART_INF_F, mx2 = -CUDART_INF_F, mx3 = -CUDART_INF_F;
       {
@@ -367,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int seg, l0;
         tile_coords(qt, p.tiles_per_seg, seg, l0);
         const int tok = l0 + row;
-        if (tok < p.seg_len) {
+        if (tok < p.seg_lens[seg]) {
           const float inv_l = 1.0f / l_run;
           __nv_bfloat16* dst = p.out + seg * p.o_ss + batch * p.o_bs + head * p.o_hs + tok * p.o_rs;
 #pragma unroll
@@ -437,14 +441,19 @@ extern "C" int erd_attn_fwd_bf16(const void* q, const void* k, const void* v,
                                  int64_t k_batch_stride, int64_t k_seg_stride,
                                  int64_t v_token_stride, int64_t v_head_stride,
                                  int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads,
-                                 int seg_len, int nseg, int head_dim, float softmax_scale,
+                                 int seg_len, int nseg, const int32_t* seg_lens, int head_dim,
+                                 float softmax_scale,
                                  void* out, int64_t o_token_stride, int64_t o_head_stride,
                                  int64_t o_batch_stride, int64_t o_seg_stride, int* status,
                                  void* stream) {
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr) return kErrNullPointer;
   if (head_dim != kHeadDim || batch <= 0 || heads <= 0 || seg_len <= 0 || nseg <= 0 ||
-      batch > 65535 || heads > 65535)
+      nseg > kMaxSegments || batch > 65535 || heads > 65535)
     return kErrBadShape;
+  if (seg_lens != nullptr) {
+    for (int s = 0; s < nseg; ++s)
+      if (seg_lens[s] <= 0 || seg_lens[s] > seg_len) return kErrBadShape;
+  }
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out)) return kErrMisaligned;
   if (!strides_ok(q_token_stride, q_head_stride, q_batch_stride, q_seg_stride) ||
       !strides_ok(k_token_stride, k_head_stride, k_batch_stride, k_seg_stride) ||
@@ -467,6 +476,8 @@ extern "C" int erd_attn_fwd_bf16(const void* q, const void* k, const void* v,
     return kErrTensorMap;
 
   AttnParams p;
+  for (int s = 0; s < kMaxSegments; ++s)
+    p.seg_lens[s] = (s < nseg) ? (seg_lens != nullptr ? seg_lens[s] : seg_len) : 0;
   p.seg_len = seg_len;
   p.nseg = nseg;
   p.tiles_per_seg = tiles_per_seg;

@@ -1,0 +1,259 @@
+"""Ulysses sequence-parallel self-attention over NCCL.
+
+The B200 equivalent of ``DistributedSequenceRank.attention``
+(``models/adapters/eraserdit/nccl_sequence.py:43-103,235-332``, Ulysses axis)
+wrapped around one EraserDiT self-attention layer
+(``models/dits/eraserdit_attention.py:242-290``).  Each of N ranks holds the
+floor-partitioned token range of the sequence (``mesh.py:163-169``) and all
+2048 channels of its tokens:
+
+1. QKV projection of the local tokens (cuBLAS);
+2. ``erd_qk_norm_rope`` normalises Q/K across all heads (the norm needs every
+   head, so it runs before the exchange), applies 3D RoPE at the tokens'
+   global grid positions, and writes Q/K/V straight into the send buffer,
+   grouped by destination rank: ``send1[dest][token][qkv][b][head % Hl][d]``
+   with Hl = H / N heads per rank (the packing copy of
+   ``layers/attention/qkv_packing.py`` disappears into the prologue);
+3. all-to-all: rank r receives every source's tokens for its Hl heads into
+   ``recv1[src][slot token][qkv][b][hl][d]`` (token-major chunks, so a
+   shorter source fills a prefix of its slot);
+4. ``erd_attn_fwd_bf16`` attends over the N received segments directly (one
+   TMA descriptor, per-segment lengths) and writes each output row into the
+   return buffer of its owner: ``send2[dest][flag | token][b][hl][d]``;
+5. inverse all-to-all; each chunk carries a leading error flag so that a
+   rank whose attention failed is reported by every peer (the protocol of
+   ``layers/attention/sequence_parallel.py:257-300``) after all ranks have
+   entered both collectives;
+6. heads are gathered back per token and ``to_out[0]`` is applied (cuBLAS).
+
+The two collectives are the only data-path communication; with CFG the
+Ulysses group is one branch's ranks (``eraserdit_b200.topology``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from . import _native
+from .layer import HEAD_DIM, HIDDEN, EraserDiTSelfAttention
+from .operator_fusion import qk_norm_rope_into
+from .sequence_sharding import floor_bounds, floor_lengths
+
+FLAG = 8  # elements reserved at the head of every returned chunk (16 bytes)
+
+
+class SequenceParallelPeerError(RuntimeError):
+    """Another rank of the Ulysses group failed between the two exchanges."""
+
+    def __init__(self, peer_ranks: tuple[int, ...]) -> None:
+        self.peer_ranks = peer_ranks
+        super().__init__("sequence-parallel attention failed on peer rank(s): "
+                         + ", ".join(str(r) for r in peer_ranks))
+
+
+Exchange = Callable[[list, list], None]
+
+
+def peer_exchange(group, group_ranks: tuple[int, ...], index: int) -> Exchange:
+    """All-to-all of per-peer contiguous chunks as one batch of point-to-point
+    sends/receives (NCCL runs the batch as one grouped launch; gloo supports it
+    too).  ``group_ranks`` are the global ranks of the group, ``index`` this
+    rank's position in it."""
+    def run(outputs: list, inputs: list) -> None:
+        ops = []
+        for i, peer in enumerate(group_ranks):
+            if i == index:
+                outputs[i].copy_(inputs[i])
+                continue
+            ops.append(dist.P2POp(dist.isend, inputs[i], peer, group))
+            ops.append(dist.P2POp(dist.irecv, outputs[i], peer, group))
+        if ops:
+            for work in dist.batch_isend_irecv(ops):
+                work.wait()
+    return run
+
+
+@dataclass
+class _Step:
+    batch: int
+    length: int
+    lengths: list
+    start: int
+    send1: torch.Tensor
+    recv1: torch.Tensor
+    send2: torch.Tensor
+    recv2: torch.Tensor
+    failed: bool = False
+
+
+class UlyssesSelfAttention:
+    """One self-attention layer with Ulysses sequence parallelism on ``degree`` ranks."""
+
+    def __init__(self, layer: EraserDiTSelfAttention, degree: int, rank: int,
+                 exchange: Exchange, group_ranks: tuple[int, ...] | None = None) -> None:
+        if layer.heads % degree:
+            raise ValueError("attention heads must be divisible by Ulysses degree")
+        if degree > 16:
+            raise ValueError("at most 16 Ulysses ranks (attention segment limit)")
+        self.layer = layer
+        self.degree = degree
+        self.rank = rank
+        self.exchange = exchange
+        self.group_ranks = group_ranks or tuple(range(degree))
+        self.local_heads = layer.heads // degree
+        self._buffers: dict[tuple, tuple] = {}
+        self.calls = 0
+
+    # ------------------------------------------------------------ partition
+    def partition(self, length: int) -> slice:
+        if length < self.degree:
+            raise ValueError("sequence length must be at least SP degree")
+        start, end = floor_bounds(length, self.degree, self.rank)
+        return slice(start, end)
+
+    def _buffers_for(self, batch: int, length: int, device, dtype):
+        key = (batch, length, device, dtype)
+        cached = self._buffers.get(key)
+        if cached is None:
+            n, hl = self.degree, self.local_heads
+            lengths = floor_lengths(length, n)
+            lmax, lme = max(lengths), lengths[self.rank]
+            row1 = 3 * batch * hl * HEAD_DIM
+            row2 = batch * hl * HEAD_DIM
+            send1 = torch.empty(n, lme, 3, batch, hl, HEAD_DIM, device=device, dtype=dtype)
+            # Zeroed once: slot rows past a shorter source's length stay finite.
+            recv1 = torch.zeros(n, lmax, 3, batch, hl, HEAD_DIM, device=device, dtype=dtype)
+            send2 = torch.zeros(n, FLAG + lmax * row2, device=device, dtype=dtype)
+            recv2 = torch.empty(n, FLAG + lme * row2, device=device, dtype=dtype)
+            cached = (lengths, send1, recv1, send2, recv2, row1, row2)
+            self._buffers[key] = cached
+        return cached
+
+    # --------------------------------------------------------------- phases
+    def pre(self, x_local: torch.Tensor, rope, length: int) -> _Step:
+        """QKV projection + fused norm/RoPE straight into the send buffer."""
+        batch = x_local.shape[0]
+        lengths, send1, recv1, send2, recv2, row1, _ = self._buffers_for(
+            batch, length, x_local.device, x_local.dtype)
+        start, end = floor_bounds(length, self.degree, self.rank)
+        if x_local.shape[1] != end - start:
+            raise ValueError("local sequence length must match the floor partition")
+        qkv = self.layer.project_qkv(x_local)
+        q, k, v = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN], qkv[..., 2 * HIDDEN:]
+        hl = self.local_heads
+        chunk = batch * hl * HEAD_DIM
+        base = send1.view(-1)
+        qk_norm_rope_into(
+            q, k, self.layer.norm_q, self.layer.norm_k, self.layer.eps, rope,
+            base[0:], base[chunk:], value=v, v_out=base[2 * chunk:], token_offset=start,
+            out_token_stride=row1, out_batch_stride=hl * HEAD_DIM, out_head_stride=HEAD_DIM,
+            heads_per_dest=hl, out_dest_stride=(end - start) * row1)
+        return _Step(batch, length, lengths, start, send1, recv1, send2, recv2)
+
+    def send_recv_1(self, step: _Step) -> tuple[list, list]:
+        outputs = [step.recv1[s, :step.lengths[s]] for s in range(self.degree)]
+        inputs = [step.send1[d] for d in range(self.degree)]
+        return outputs, inputs
+
+    def attend(self, step: _Step) -> None:
+        """Attention over the received segments; rows go to their owners' chunks."""
+        try:
+            self._attend(step)
+            step.send2[:, :FLAG].zero_()
+        except Exception:
+            step.failed = True
+            step.send2[:, :FLAG].fill_(1.0)
+            raise
+        finally:
+            self.calls += 1
+
+    def _attend(self, step: _Step) -> None:
+        n, hl, b = self.degree, self.local_heads, step.batch
+        lmax = max(step.lengths)
+        row1 = 3 * b * hl * HEAD_DIM
+        chunk = b * hl * HEAD_DIM
+        r = step.recv1.view(-1)
+        o = step.send2.view(-1)[FLAG:]
+        lib = _native.load()
+        lens = (ctypes.c_int32 * n)(*step.lengths)
+        strides = [row1, HEAD_DIM, hl * HEAD_DIM, lmax * row1]  # token, head, batch, segment
+        device = step.recv1.device
+        with torch.cuda.device(device):
+            rc = lib.erd_attn_fwd_bf16(
+                r.data_ptr(), r[chunk:].data_ptr(), r[2 * chunk:].data_ptr(),
+                *strides, *strides, *strides, b, hl, lmax, n, lens, HEAD_DIM,
+                float(self.layer.softmax_scale), o.data_ptr(),
+                b * hl * HEAD_DIM, HEAD_DIM, hl * HEAD_DIM, FLAG + lmax * b * hl * HEAD_DIM,
+                _native.status_word(device).data_ptr(), _native.stream_handle(device))
+        _native.check(rc, "erd_attn_fwd_bf16")
+
+    def send_recv_2(self, step: _Step) -> tuple[list, list]:
+        row2 = step.batch * self.local_heads * HEAD_DIM
+        outputs = [step.recv2[s] for s in range(self.degree)]
+        inputs = [step.send2[d, :FLAG + step.lengths[d] * row2] for d in range(self.degree)]
+        return outputs, inputs
+
+    def post(self, step: _Step) -> torch.Tensor:
+        """Peer error check, head gather, output projection."""
+        flags = step.recv2[:, 0].float()
+        if step.failed:
+            raise RuntimeError("local sequence-parallel attention failed")
+        bad = torch.nonzero(flags != 0).flatten().tolist()
+        if bad:
+            raise SequenceParallelPeerError(tuple(self.group_ranks[i] for i in bad))
+        lme = step.lengths[self.rank]
+        n, hl, b = self.degree, self.local_heads, step.batch
+        heads = step.recv2[:, FLAG:].view(n, lme, b, hl, HEAD_DIM)
+        attn = heads.permute(2, 1, 0, 3, 4).reshape(b, lme, n * hl * HEAD_DIM)
+        return self.layer.project_out(attn)
+
+    # -------------------------------------------------------------- forward
+    def forward(self, x_local: torch.Tensor, rope, length: int) -> torch.Tensor:
+        """Layer output for this rank's tokens [B, L_rank, 2048]."""
+        step = self.pre(x_local, rope, length)
+        out1, in1 = self.send_recv_1(step)
+        self.exchange(out1, in1)
+        error = None
+        try:
+            self.attend(step)
+        except Exception as exc:  # every rank still enters the second exchange
+            error = exc
+        out2, in2 = self.send_recv_2(step)
+        self.exchange(out2, in2)
+        if error is not None:
+            raise error
+        return self.post(step)
+
+    __call__ = forward
+
+
+def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, rope
+                  ) -> list[torch.Tensor]:
+    """Run all ``degree`` ranks of the Ulysses layer inside one process on one
+    device, exchanging chunks by copies (the same buffers and kernels as the
+    NCCL path).  Returns each rank's output; used to check the data layout on
+    a single GPU."""
+    length = x.shape[1]
+    ranks = [UlyssesSelfAttention(layer, degree, r, exchange=None) for r in range(degree)]
+    steps = []
+    for r in ranks:
+        sl = r.partition(length)
+        steps.append(r.pre(x[:, sl].contiguous(), rope, length))
+
+    def all_to_all(pairs):
+        for dst in range(degree):
+            outputs, _ = pairs[dst]
+            for src in range(degree):
+                outputs[src].copy_(pairs[src][1][dst])
+
+    all_to_all([r.send_recv_1(s) for r, s in zip(ranks, steps)])
+    for r, s in zip(ranks, steps):
+        r.attend(s)
+    all_to_all([r.send_recv_2(s) for r, s in zip(ranks, steps)])
+    return [r.post(s) for r, s in zip(ranks, steps)]

@@ -89,8 +89,12 @@ int erd_qk_norm_rope(const void* q_in, const void* k_in, const void* v_in,
  * called from models/dits/eraserdit_attention.py:287-289 and from the Ulysses
  * path after the sequence-to-head exchange (nccl_sequence.py:259-260).
  *
- * The sequence of every (batch, head) is `nseg` segments of `seg_len` tokens
- * (nseg = 1 for one GPU; one segment per source rank after the all-to-all).
+ * The sequence of every (batch, head) is `nseg` (<= 16) segments held in
+ * slots of `seg_len` tokens; segment s holds seg_lens[s] valid tokens
+ * (seg_lens: host array of nseg entries, or NULL for all seg_len).  nseg = 1
+ * on one GPU; after the Ulysses all-to-all there is one segment per source
+ * rank.  Rows past a segment's valid length are never attended to or
+ * written; they must hold finite values (e.g. zeros).
  * Element (b, h, segment s, token t, d) of X in {q, k, v} is at
  *   X + s*x_seg_stride + b*x_batch_stride + h*x_head_stride + t*x_token_stride + d,
  * and the output row goes to the same formula with the o_* strides.
@@ -101,7 +105,8 @@ int erd_attn_fwd_bf16(const void* q, const void* k, const void* v, int64_t q_tok
                       int64_t k_token_stride, int64_t k_head_stride, int64_t k_batch_stride,
                       int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
                       int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads,
-                      int seg_len, int nseg, int head_dim, float softmax_scale, void* out,
+                      int seg_len, int nseg, const int32_t* seg_lens, int head_dim,
+                      float softmax_scale, void* out,
                       int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride,
                       int64_t o_seg_stride, int* status, void* stream);
 

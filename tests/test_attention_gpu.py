@@ -78,7 +78,7 @@ def test_segmented_sequence():
     strides = [64, seg_len * 64, heads * seg_len * 64, ss]
     rc = lib.erd_attn_fwd_bf16(
         recv[:, 0].data_ptr(), recv[:, 1].data_ptr(), recv[:, 2].data_ptr(), *strides, *strides,
-        *strides, batch, heads, seg_len, nseg, 64, 0.125, out.data_ptr(),
+        *strides, batch, heads, seg_len, nseg, None, 64, 0.125, out.data_ptr(),
         heads * 64, 64, seg_len * heads * 64, batch * seg_len * heads * 64,
         _native.status_word(q.device).data_ptr(), _native.stream_handle(q.device))
     _native.check(rc, "erd_attn_fwd_bf16")

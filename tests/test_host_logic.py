@@ -1,0 +1,40 @@
+"""Shard plans and rank topology reproduce the reference's (golden JSON)."""
+import pytest
+
+from eraserdit_b200.sequence_sharding import floor_lengths, plan_sequence_shards
+from eraserdit_b200.topology import DiTTopology
+
+
+def test_shard_plans_match_reference(golden_host):
+    for key, rows in golden_host["plans"].items():
+        length, degree = map(int, key.split("_"))
+        got = [[p.global_length, p.padded_length, p.local_start, p.local_end,
+                p.valid_local_length, p.pad_right] for p in plan_sequence_shards(length, degree, 0)]
+        assert got == rows, key
+
+
+def test_floor_lengths_match_reference(golden_host):
+    for key, lengths in golden_host["floor_lengths"].items():
+        length, degree = map(int, key.split("_"))
+        assert floor_lengths(length, degree) == lengths
+
+
+def test_topologies_match_reference(golden_host):
+    topos = {"sp8": DiTTopology(ulysses=8), "cfg2_sp4": DiTTopology(ulysses=4, cfg=2),
+             "cfg2_sp2": DiTTopology(ulysses=2, cfg=2)}
+    for name, topo in topos.items():
+        ref = golden_host["topology"][name]
+        for axis in ("ulysses", "sp", "cfg"):
+            assert [list(g) for g in topo.groups(axis)] == ref[axis], (name, axis)
+        assert [list(topo.coordinates(r)) for r in range(topo.world_size)] == ref["coordinates"]
+
+
+def test_plan_validation_errors():
+    with pytest.raises(ValueError):
+        plan_sequence_shards(10, 0, 0)
+    with pytest.raises(ValueError):
+        plan_sequence_shards(10, 2, 2)
+    with pytest.raises(TypeError):
+        plan_sequence_shards(10.0, 2, 0)
+    with pytest.raises(ValueError):
+        DiTTopology(cfg=3)
