@@ -123,7 +123,7 @@ class ClockSampler:
 # ------------------------------------------------------------- CPU sample
 def cpu_sample_step(threads: int):
     """1/64 of the config-1 layer through the oracle (the reference's CPU path):
-    the four projections for 510 of the 65280 tokens, their QK RMSNorm + RoPE,
+    the four projections for 1020 of the 65280 tokens, their QK RMSNorm + RoPE,
     and one (batch, head) of attention over the full 32640-token sequence."""
     from oracle import reference_path as ref
     torch.set_num_threads(threads)
@@ -151,7 +151,7 @@ def cpu_sample_step(threads: int):
                         f"(batch, head) of fp32 SDPA over {SEQ} tokens")
 
 
-def cpu_baseline(steps: int = 3) -> dict:
+def cpu_baseline(steps: int = 12) -> dict:
     threads = os.cpu_count() or 1
     step, flop, sample = cpu_sample_step(threads)
     step()
