@@ -223,18 +223,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s1 = (j + 1) % kStages;
         const uint32_t ph1 = ((j + 1) / kStages) & 1;
         const bool more = j + 1 < n_kv;
+        // Operand waits first (normally long complete), so that once a
+        // softmax hands over its P the products are issued without delay.
+        if (more && !mbar_wait(smem_u32(&bars->k_full[s1]), ph1, abort, p.status, kStatusTimeoutMma))
+          break;
+        if (!mbar_wait(smem_u32(&bars->v_full[s]), ph, abort, p.status, kStatusTimeoutMma)) break;
         // query tile A
         if (!mbar_wait(smem_u32(&bars->p_full[0]), j & 1, abort, p.status, kStatusTimeoutMma)) break;
         tc_fence_after();
         if (more) {
-          if (!mbar_wait(smem_u32(&bars->k_full[s1]), ph1, abort, p.status, kStatusTimeoutMma))
-            break;
-          tc_fence_after();
           issue_qk(0, s1);
           mma_commit(smem_u32(&bars->s_full[0]));
         }
-        if (!mbar_wait(smem_u32(&bars->v_full[s]), ph, abort, p.status, kStatusTimeoutMma)) break;
-        tc_fence_after();
         issue_pv(0, s, j > 0);
         mma_commit(smem_u32(&bars->o_done[0]));
         // query tile B
