@@ -189,12 +189,13 @@ def run_reference(args, rank: int) -> None:
 
 
 # ------------------------------------------------------------ GPU arm
-def build_problem(device):
+def build_problem(device, precision: str = "bf16"):
     from eraserdit_b200.layer import EraserDiTSelfAttention
     from eraserdit_b200.rotary import LTXVideoRotaryPosEmbed
     from oracle.inputs import make_params  # seeded synthetic weights (same generator as tests)
     params = make_params(1, EPS, device=device)
-    layer = EraserDiTSelfAttention.from_params(params.to(torch.bfloat16), device=device)
+    layer = EraserDiTSelfAttention.from_params(params.to(torch.bfloat16), device=device,
+                                               precision=precision)
     rope = LTXVideoRotaryPosEmbed()(FRAMES, HEIGHT, WIDTH, device=device)
     return layer, rope
 
@@ -203,7 +204,8 @@ def run_single(args) -> None:
     from eraserdit_b200 import _native
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
-    layer, rope = build_problem(device)
+    precision = "fp8" if args.fp8 else "bf16"
+    layer, rope = build_problem(device, precision)
     g = torch.Generator(device=device).manual_seed(1)
     x = torch.randn(BATCH, SEQ, HIDDEN, generator=g, device=device).bfloat16()
     stream = torch.cuda.current_stream(device)
@@ -224,7 +226,7 @@ def run_single(args) -> None:
             e0.record(stream)
         attention_bshd(q.unflatten(2, (HEADS, HEAD_DIM)), k.unflatten(2, (HEADS, HEAD_DIM)),
                        v.unflatten(2, (HEADS, HEAD_DIM)), layer.softmax_scale,
-                       out=attn_out.unflatten(2, (HEADS, HEAD_DIM)))
+                       out=attn_out.unflatten(2, (HEADS, HEAD_DIM)), precision=precision)
         if record:
             e1.record(stream)
             attn_events.append((e0, e1))
@@ -264,20 +266,24 @@ def run_single(args) -> None:
     peaks, peak_src = measured_peaks()
     timed_s = ms * args.steps / 1e3
     peak_key = "bf16_tflops_sustained" if timed_s >= 1.0 else "bf16_tflops"
+    peak = peaks[peak_key]
+    if args.fp8:  # dense FP8 runs at twice the BF16 rate on this part
+        peak, peak_key = 2 * peak, f"2 x {peak_key} (dense fp8 = 2x bf16)"
     achieved = ATTN_FLOP / (core_ms / 1e3) / 1e12
     clock = clocks.summary()
     line = {
         "metric": METRIC, "value": LAYER_FLOP / (ms / 1e3) / 1e12, "unit": UNIT, "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": BATCH, "seq_len": SEQ,
-                   "parallelism": "sp1",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "e4m3/bf16" if args.fp8 else "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD + (", FP8 attention (configuration 3 numerics)"
+                                           if args.fp8 else ""),
+                   "global_batch": BATCH, "seq_len": SEQ, "parallelism": "sp1",
                    "l2": "inputs larger than L2 (x 267 MB, QKV 802 MB per step)"},
         "layer_tflop": LAYER_FLOP / 1e12,
-        "roofline": {"kernel": "attn_fwd_bf16", "bound": "tensor",
-                     "achieved": achieved, "peak": peaks[peak_key], "unit": UNIT,
-                     "frac": achieved / peaks[peak_key],
+        "roofline": {"kernel": "attn_fwd_fp8 (+ fp8 quantize)" if args.fp8 else "attn_fwd_bf16",
+                     "bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
+                     "frac": achieved / peak,
                      "peak_source": f"{peak_src} {peak_key}",
                      "traffic": profiled_traffic("attn_fwd_bf16_config1"),
                      "kernel_ms": core_ms},
@@ -285,7 +291,7 @@ def run_single(args) -> None:
                 "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": host_x.numel() * host_x.element_size(),
                 "d2h_bytes_per_step": host_y.numel() * host_y.element_size()},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": (4 if args.fp8 else 2) * args.steps,
         "clocks": clock,
     }
     if not args.no_cpu_baseline:
@@ -301,6 +307,8 @@ def main() -> None:
     parser.add_argument("--impl", default="native", choices=["native", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cfg", type=int, default=1, help="CFG branches on separate rank groups")
+    parser.add_argument("--fp8", action="store_true",
+                        help="Sage-style FP8 attention (configuration 3) instead of BF16")
     args = parser.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":

@@ -36,7 +36,12 @@ SIGNATURES = {
     "erd_attn_fwd_bf16": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 4 + [_vp, _c_int, _c_float,
                                                                             _vp] + [_c_i64] * 4
                          + [_vp, _vp],
+    "erd_attn_fp8_workspace_bytes": [_c_int, _c_int, _c_int, _c_int],
+    "erd_attn_fwd_fp8": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 4 + [_vp, _c_int, _c_float,
+                                                                           _vp] + [_c_i64] * 4
+                        + [_vp, ctypes.c_size_t, _vp, _vp],
 }
+RESTYPES = {"erd_error_string": ctypes.c_char_p, "erd_attn_fp8_workspace_bytes": ctypes.c_size_t}
 
 _lib = None
 _lock = threading.Lock()
@@ -59,7 +64,7 @@ def load() -> ctypes.CDLL:
         for name, argtypes in SIGNATURES.items():
             fn = getattr(lib, name)
             fn.argtypes = argtypes
-            fn.restype = ctypes.c_char_p if name == "erd_error_string" else ctypes.c_int
+            fn.restype = RESTYPES.get(name, ctypes.c_int)
         if lib.erd_abi_version() != ABI_VERSION:
             raise RuntimeError(
                 f"eraserdit_b200 ABI mismatch: library {lib.erd_abi_version()}, "
@@ -98,6 +103,22 @@ def read_status(device: torch.device, reset: bool = True) -> int:
     if reset and value:
         word.zero_()
     return value
+
+
+_workspaces: dict[int, torch.Tensor] = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> int:
+    """Address of a caller-owned, 1024-byte aligned device buffer of at least
+    ``nbytes`` (grown on demand, reused across calls on this device's stream
+    order)."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _workspaces.get(index)
+    if buf is None or buf.numel() < nbytes + 1024:
+        buf = torch.empty(nbytes + 1024, dtype=torch.uint8, device=torch.device("cuda", index))
+        _workspaces[index] = buf
+    base = buf.data_ptr()
+    return (base + 1023) // 1024 * 1024
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

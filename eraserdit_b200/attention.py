@@ -33,6 +33,7 @@ class AttentionBackendEnum(str, Enum):
     SAGE_ATTN = "sage_attn"
     SAGE_FP8 = "sage_fp8"
     B200_NATIVE = "b200_native"
+    B200_FP8 = "b200_fp8"
 
 
 @dataclass(frozen=True)
@@ -185,14 +186,44 @@ def _check_operand(name: str, t: torch.Tensor) -> None:
         raise ValueError(f"{name} needs 16-byte aligned rows (strides multiple of 8 elements)")
 
 
+def _segmented_call(fn_name: str, query, key, value, out, softmax_scale, *, batch, heads,
+                    seg_len, nseg, seg_lens, q_strides, k_strides, v_strides, o_strides,
+                    extra=()) -> None:
+    """Enqueue an attention entry point with segmented strides (token, head,
+    batch, segment) for q / k / v / out."""
+    lib = _native.load()
+    device = query.device
+    lens = None
+    if seg_lens is not None:
+        import ctypes
+        lens = (ctypes.c_int32 * nseg)(*seg_lens)
+    with torch.cuda.device(device):
+        rc = getattr(lib, fn_name)(
+            query.data_ptr(), key.data_ptr(), value.data_ptr(), *q_strides, *k_strides,
+            *v_strides, batch, heads, seg_len, nseg, lens, 64, float(softmax_scale),
+            out.data_ptr(), *o_strides, *extra,
+            _native.status_word(device).data_ptr(), _native.stream_handle(device))
+    _native.check(rc, fn_name)
+
+
+def fp8_workspace(device: torch.device, batch: int, heads: int, seg_len: int, nseg: int) -> tuple:
+    lib = _native.load()
+    nbytes = int(lib.erd_attn_fp8_workspace_bytes(batch, heads, seg_len, nseg))
+    return _native.workspace(device, nbytes), nbytes
+
+
 def attention_bshd(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
-                   softmax_scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
-    """softmax(Q K^T * scale) V on BSHD tensors through ``erd_attn_fwd_bf16``."""
+                   softmax_scale: float, out: torch.Tensor | None = None,
+                   precision: str = "bf16") -> torch.Tensor:
+    """softmax(Q K^T * scale) V on BSHD tensors through ``erd_attn_fwd_bf16``
+    (or ``erd_attn_fwd_fp8`` with ``precision="fp8"``)."""
     validate_bshd_qkv(query, key, value)
     if query.shape != key.shape:
         raise ValueError("b200_native self-attention needs equal Q and K/V shapes")
     if query.dtype != torch.bfloat16 or not query.is_cuda or query.shape[-1] != 64:
         raise ValueError("b200_native needs CUDA bfloat16 BSHD tensors with head_dim 64")
+    if precision not in ("bf16", "fp8"):
+        raise ValueError("precision must be bf16 or fp8")
     batch, seq, heads, dim = query.shape
     if out is None:
         out = torch.empty_like(query, memory_format=torch.contiguous_format)
@@ -200,17 +231,14 @@ def attention_bshd(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
         _check_operand(name, t)
     if seq == 0 or batch == 0:
         return out
-    lib = _native.load()
-    device = query.device
-    qs, ks, vs, os_ = query.stride(), key.stride(), value.stride(), out.stride()
-    with torch.cuda.device(device):
-        rc = lib.erd_attn_fwd_bf16(
-            query.data_ptr(), key.data_ptr(), value.data_ptr(),
-            qs[1], qs[2], qs[0], 0, ks[1], ks[2], ks[0], 0, vs[1], vs[2], vs[0], 0,
-            batch, heads, seq, 1, None, dim, float(softmax_scale),
-            out.data_ptr(), os_[1], os_[2], os_[0], 0,
-            _native.status_word(device).data_ptr(), _native.stream_handle(device))
-    _native.check(rc, "erd_attn_fwd_bf16")
+    st = lambda t: (t.stride(1), t.stride(2), t.stride(0), 0)
+    extra = ()
+    if precision == "fp8":
+        extra = fp8_workspace(query.device, batch, heads, seq, 1)
+    _segmented_call("erd_attn_fwd_bf16" if precision == "bf16" else "erd_attn_fwd_fp8",
+                    query, key, value, out, softmax_scale, batch=batch, heads=heads, seg_len=seq,
+                    nseg=1, seg_lens=None, q_strides=st(query), k_strides=st(key),
+                    v_strides=st(value), o_strides=st(out), extra=extra)
     return out
 
 
@@ -237,3 +265,54 @@ class B200AttentionImpl(AttentionImpl):
 
     def report(self) -> dict:
         return {"backend": "b200_native", "calls": self.calls}
+
+
+class B200FP8AttentionBackend(AttentionBackend):
+    """SageAttention-style FP8 attention (E4M3 Q/K/P/V, FP32 accumulation) for sm_100a."""
+
+    accept_output_buffer: bool = True
+
+    @staticmethod
+    def probe(capability: AttentionCapability) -> AttentionSupport:
+        return B200AttentionBackend.probe(capability)
+
+    @staticmethod
+    def get_supported_head_sizes() -> list[int]:
+        return [64]
+
+    @staticmethod
+    def get_enum() -> AttentionBackendEnum:
+        return AttentionBackendEnum.B200_FP8
+
+    @staticmethod
+    def get_impl_cls() -> type["B200FP8AttentionImpl"]:
+        return B200FP8AttentionImpl
+
+
+class B200FP8AttentionImpl(B200AttentionImpl):
+    """Drop-in for ``SageFP8AttentionImpl`` (``layers/attention/backends/sage_fp8.py:100-219``):
+    same constructor arguments (``pv_accum_dtype`` must be FP32 accumulation;
+    the quantization granularity is the per-128-token-block scheme)."""
+
+    def __init__(self, num_heads: int, head_size: int, softmax_scale: float, causal: bool = False,
+                 num_kv_heads: int | None = None, prefix: str = "",
+                 pv_accum_dtype: str = "fp32+fp32", qk_quant_gran: str = "per_block",
+                 **extra_impl_args) -> None:
+        if pv_accum_dtype != "fp32+fp32":
+            raise ValueError("b200_fp8 accumulates P V in FP32 only")
+        if qk_quant_gran not in ("per_block", "per_thread", "per_warp"):
+            raise ValueError("unsupported QK quantization granularity")
+        super().__init__(num_heads, head_size, softmax_scale, causal, num_kv_heads, prefix,
+                         **extra_impl_args)
+        self.pv_accum_dtype = pv_accum_dtype
+        self.qk_quant_gran = "per_block"
+
+    def forward(self, query, key, value, attn_metadata) -> torch.Tensor:
+        if attn_metadata is not None and getattr(attn_metadata, "attn_mask", None) is not None:
+            raise ValueError("b200_fp8 attention does not take an attention mask")
+        self.calls += 1
+        return attention_bshd(query, key, value, self.softmax_scale, precision="fp8")
+
+    def report(self) -> dict:
+        return {"backend": "b200_fp8", "calls": self.calls, "qk_quant_granularity": "per_block",
+                "pv_accum_dtype": self.pv_accum_dtype, "smooth_k": True}

@@ -37,7 +37,7 @@ def run_sequence_parallel(args) -> None:
         groups = DiTGroups(topo)
         group, ranks, index = groups.get("ulysses") if world // cfg > 1 else (None, (rank,), 0)
         cfg_index = topo.coordinates(rank)[3]
-        layer, rope = B.build_problem(device)
+        layer, rope = B.build_problem(device, "fp8" if args.fp8 else "bf16")
         g = torch.Generator(device=device).manual_seed(1)
         x_full = torch.randn(B.BATCH, B.SEQ, B.HIDDEN, generator=g, device=device).bfloat16()
         per_branch = B.BATCH // cfg
@@ -102,6 +102,9 @@ def run_sequence_parallel(args) -> None:
                 raise RuntimeError(f"kernel wait timed out on some rank (status {int(status)})")
             peaks, src = B.measured_peaks()
             peak_key = "bf16_tflops_sustained" if ms * args.steps >= 1000 else "bf16_tflops"
+            peak = peaks[peak_key]
+            if args.fp8:
+                peak, peak_key = 2 * peak, f"2 x {peak_key} (dense fp8 = 2x bf16)"
             local_attn_flop = B.ATTN_FLOP / world
             achieved = local_attn_flop / (kernel_ms / 1e3) / 1e12
             parallelism = f"cfg{cfg}xsp{world // cfg}" if cfg > 1 else f"sp{world}"
@@ -109,21 +112,22 @@ def run_sequence_parallel(args) -> None:
                 "metric": B.METRIC, "value": B.LAYER_FLOP / (ms / 1e3) / 1e12, "unit": B.UNIT,
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "bf16", "data": "synthetic",
+                "dtype": "e4m3/bf16" if args.fp8 else "bf16", "data": "synthetic",
                 "config": {"workload": B.WORKLOAD.replace("config 1", "config 2 (Ulysses SP)"),
                            "global_batch": B.BATCH, "seq_len": B.SEQ, "parallelism": parallelism,
                            "l2": "inputs larger than L2"},
                 "layer_tflop": B.LAYER_FLOP / 1e12,
-                "roofline": {"kernel": "attn_fwd_bf16 (per rank, max over ranks)",
-                             "bound": "tensor", "achieved": achieved, "peak": peaks[peak_key],
-                             "unit": B.UNIT, "frac": achieved / peaks[peak_key],
+                "roofline": {"kernel": ("attn_fwd_fp8" if args.fp8 else "attn_fwd_bf16")
+                             + " (per rank, max over ranks)",
+                             "bound": "tensor", "achieved": achieved, "peak": peak,
+                             "unit": B.UNIT, "frac": achieved / peak,
                              "peak_source": f"{src} {peak_key}",
                              "traffic": None, "kernel_ms": kernel_ms},
                 "e2e": {"value": B.LAYER_FLOP / (e2e_ms / 1e3) / 1e12, "unit": B.UNIT,
                         "ms_per_step": e2e_ms,
                         "h2d_bytes_per_step": host_x.numel() * host_x.element_size() * world,
                         "d2h_bytes_per_step": host_y.numel() * host_y.element_size() * world},
-                "gpu_launches": 2 * args.steps,
+                "gpu_launches": (4 if args.fp8 else 2) * args.steps,
                 "clocks": clock,
             }), flush=True)
     finally:

@@ -10,7 +10,9 @@ output projection.  Data movement in HBM:
 2. ``erd_qk_norm_rope`` normalises and rotates Q and K in place in that
    buffer (one read + one write of Q and K);
 3. ``erd_attn_fwd_bf16`` reads Q/K/V straight from the interleaved buffer via
-   TMA (token stride 6144) and writes O in [B, S, H*D] order;
+   TMA (token stride 6144) and writes O in [B, S, H*D] order (or, with
+   ``precision="fp8"``, ``erd_attn_fwd_fp8`` quantises them into its
+   workspace first);
 4. one cuBLAS GEMM applies ``to_out[0]``.
 """
 
@@ -31,7 +33,7 @@ HEAD_DIM = 64
 class EraserDiTSelfAttention:
     def __init__(self, wq, bq, wk, bk, wv, bv, wo, bo, norm_q, norm_k, eps: float,
                  heads: int = HEADS, device: torch.device | str = "cuda",
-                 dtype: torch.dtype = torch.bfloat16) -> None:
+                 dtype: torch.dtype = torch.bfloat16, precision: str = "bf16") -> None:
         device = torch.device(device)
         kw = dict(device=device, dtype=dtype)
         if heads * HEAD_DIM != HIDDEN:
@@ -48,12 +50,15 @@ class EraserDiTSelfAttention:
         self.norm_k = None if norm_k is None else norm_k.to(**kw).contiguous()
         self.softmax_scale = HEAD_DIM ** -0.5
         self.device = device
+        if precision not in ("bf16", "fp8"):
+            raise ValueError("precision must be bf16 or fp8")
+        self.precision = precision
 
     @classmethod
-    def from_params(cls, p, device="cuda") -> "EraserDiTSelfAttention":
+    def from_params(cls, p, device="cuda", precision: str = "bf16") -> "EraserDiTSelfAttention":
         """From an object with wq, bq, ..., norm_q, norm_k, eps attributes."""
         return cls(p.wq, p.bq, p.wk, p.bk, p.wv, p.bv, p.wo, p.bo, p.norm_q, p.norm_k, p.eps,
-                   device=device)
+                   device=device, precision=precision)
 
     @classmethod
     def from_attention_module(cls, attn, device="cuda") -> "EraserDiTSelfAttention":
@@ -75,7 +80,7 @@ class EraserDiTSelfAttention:
             out = torch.empty(batch, seq, HIDDEN, device=qkv.device, dtype=qkv.dtype)
         attention_bshd(q.unflatten(2, (self.heads, HEAD_DIM)), k.unflatten(2, (self.heads, HEAD_DIM)),
                        v.unflatten(2, (self.heads, HEAD_DIM)), self.softmax_scale,
-                       out=out.unflatten(2, (self.heads, HEAD_DIM)))
+                       out=out.unflatten(2, (self.heads, HEAD_DIM)), precision=self.precision)
         return out
 
     def project_out(self, attn: torch.Tensor) -> torch.Tensor:

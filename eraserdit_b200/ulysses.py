@@ -32,7 +32,6 @@ Ulysses group is one branch's ranks (``eraserdit_b200.topology``).
 
 from __future__ import annotations
 
-import ctypes
 from dataclasses import dataclass
 from typing import Callable
 
@@ -174,24 +173,21 @@ class UlyssesSelfAttention:
             self.calls += 1
 
     def _attend(self, step: _Step) -> None:
+        from .attention import _segmented_call, fp8_workspace
         n, hl, b = self.degree, self.local_heads, step.batch
         lmax = max(step.lengths)
         row1 = 3 * b * hl * HEAD_DIM
         chunk = b * hl * HEAD_DIM
         r = step.recv1.view(-1)
         o = step.send2.view(-1)[FLAG:]
-        lib = _native.load()
-        lens = (ctypes.c_int32 * n)(*step.lengths)
-        strides = [row1, HEAD_DIM, hl * HEAD_DIM, lmax * row1]  # token, head, batch, segment
-        device = step.recv1.device
-        with torch.cuda.device(device):
-            rc = lib.erd_attn_fwd_bf16(
-                r.data_ptr(), r[chunk:].data_ptr(), r[2 * chunk:].data_ptr(),
-                *strides, *strides, *strides, b, hl, lmax, n, lens, HEAD_DIM,
-                float(self.layer.softmax_scale), o.data_ptr(),
-                b * hl * HEAD_DIM, HEAD_DIM, hl * HEAD_DIM, FLAG + lmax * b * hl * HEAD_DIM,
-                _native.status_word(device).data_ptr(), _native.stream_handle(device))
-        _native.check(rc, "erd_attn_fwd_bf16")
+        strides = (row1, HEAD_DIM, hl * HEAD_DIM, lmax * row1)  # token, head, batch, segment
+        o_strides = (b * hl * HEAD_DIM, HEAD_DIM, hl * HEAD_DIM, FLAG + lmax * b * hl * HEAD_DIM)
+        fp8 = self.layer.precision == "fp8"
+        extra = fp8_workspace(r.device, b, hl, lmax, n) if fp8 else ()
+        _segmented_call("erd_attn_fwd_fp8" if fp8 else "erd_attn_fwd_bf16", r, r[chunk:],
+                        r[2 * chunk:], o, self.layer.softmax_scale, batch=b, heads=hl,
+                        seg_len=lmax, nseg=n, seg_lens=step.lengths, q_strides=strides,
+                        k_strides=strides, v_strides=strides, o_strides=o_strides, extra=extra)
 
     def send_recv_2(self, step: _Step) -> tuple[list, list]:
         row2 = step.batch * self.local_heads * HEAD_DIM

@@ -19,6 +19,7 @@
 #ifndef ERASERDIT_B200_H_
 #define ERASERDIT_B200_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -109,6 +110,30 @@ int erd_attn_fwd_bf16(const void* q, const void* k, const void* v, int64_t q_tok
                       float softmax_scale, void* out,
                       int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride,
                       int64_t o_seg_stride, int* status, void* stream);
+
+/*
+ * SageAttention-style FP8 attention, head_dim 64: K smoothed by its per-head
+ * token mean, Q and K quantised to E4M3 per 128-token block, V to E4M3 per
+ * channel, P to E4M3 (scaled by 448), FP32 accumulation (tcgen05
+ * kind::f8f6f4).  Replaces SageFP8AttentionImpl.forward
+ * (layers/attention/backends/sage_fp8.py:174-219) with its peripheral
+ * quantization (layers/attention/backends/sage_peripheral.py:33-81).
+ * Inputs, sequence segments and output use exactly the addressing of
+ * erd_attn_fwd_bf16.  `workspace` (1024-byte aligned, at least
+ * erd_attn_fp8_workspace_bytes(...) bytes, caller-owned) receives the
+ * quantised operands and scales; the call does not allocate.
+ */
+size_t erd_attn_fp8_workspace_bytes(int batch, int heads, int seg_len, int nseg);
+
+int erd_attn_fwd_fp8(const void* q, const void* k, const void* v, int64_t q_token_stride,
+                     int64_t q_head_stride, int64_t q_batch_stride, int64_t q_seg_stride,
+                     int64_t k_token_stride, int64_t k_head_stride, int64_t k_batch_stride,
+                     int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+                     int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads,
+                     int seg_len, int nseg, const int32_t* seg_lens, int head_dim,
+                     float softmax_scale, void* out, int64_t o_token_stride,
+                     int64_t o_head_stride, int64_t o_batch_stride, int64_t o_seg_stride,
+                     void* workspace, size_t workspace_bytes, int* status, void* stream);
 
 #ifdef __cplusplus
 }
