@@ -40,6 +40,8 @@ SIGNATURES = {
     "erd_attn_fwd_fp8": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 4 + [_vp, _c_int, _c_float,
                                                                            _vp] + [_c_i64] * 4
                         + [_vp, ctypes.c_size_t, _vp, _vp],
+    "erd_attn_fwd_fp8_static_scratch": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 4
+                                       + [_vp, _c_int, _c_float, _vp] + [_c_i64] * 4 + [_vp, _vp],
 }
 RESTYPES = {"erd_error_string": ctypes.c_char_p, "erd_attn_fp8_workspace_bytes": ctypes.c_size_t}
 

@@ -135,6 +135,33 @@ int erd_attn_fwd_fp8(const void* q, const void* k, const void* v, int64_t q_toke
                      int64_t o_head_stride, int64_t o_batch_stride, int64_t o_seg_stride,
                      void* workspace, size_t workspace_bytes, int* status, void* stream);
 
+/*
+ * erd_attn_fwd_fp8 without a caller workspace.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory when
+ * they run attention (a host on the plain C ABI without a caching allocator,
+ * where each cudaMalloc would synchronise the device, or a server whose HBM
+ * budget is fixed at start-up).  The workspace is a static device array of
+ * the library; the call allocates nothing.
+ *   - Shapes needing more than ERD_FP8_STATIC_SCRATCH_BYTES of workspace
+ *     (erd_attn_fp8_workspace_bytes) return -6 before anything is enqueued.
+ *   - The first call on a device looks up the array's address with that
+ *     device current; make it before any stream capture.
+ *   - All calls on a device share the array: calls that may overlap in time
+ *     (other streams, unordered host threads) race on it.
+ *   - Nothing in the array needs to start at zero.
+ * Arguments and results are those of erd_attn_fwd_fp8.
+ */
+#define ERD_FP8_STATIC_SCRATCH_BYTES ((size_t)64 << 20)
+
+int erd_attn_fwd_fp8_static_scratch(
+    const void* q, const void* k, const void* v, int64_t q_token_stride, int64_t q_head_stride,
+    int64_t q_batch_stride, int64_t q_seg_stride, int64_t k_token_stride, int64_t k_head_stride,
+    int64_t k_batch_stride, int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+    int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads, int seg_len, int nseg,
+    const int32_t* seg_lens, int head_dim, float softmax_scale, void* out,
+    int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride, int64_t o_seg_stride,
+    int* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
