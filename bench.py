@@ -192,7 +192,7 @@ def run_reference(args, rank: int) -> None:
 def build_problem(device, precision: str = "bf16"):
     from eraserdit_b200.layer import EraserDiTSelfAttention
     from eraserdit_b200.rotary import LTXVideoRotaryPosEmbed
-    from oracle.inputs import make_params  # seeded synthetic weights (same generator as tests)
+    from eraserdit_b200.synthetic import make_params  # seeded synthetic weights
     params = make_params(1, EPS, device=device)
     layer = EraserDiTSelfAttention.from_params(params.to(torch.bfloat16), device=device,
                                                precision=precision)
