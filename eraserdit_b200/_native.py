@@ -19,7 +19,7 @@ from pathlib import Path
 import torch
 
 LIBRARY_PATH = Path(__file__).resolve().parent / "liberaserdit_b200.so"
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _c_int, _c_i64, _c_float, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -31,11 +31,16 @@ SIGNATURES = {
                             _c_float, _c_float, _c_float, _c_float, _c_float, _c_float, _vp, _vp],
     "erd_qk_norm_rope": [_vp, _vp, _vp, _c_i64, _c_i64, _c_int, _c_int, _c_int, _vp, _vp,
                          _c_float, _c_int, _vp, _vp, _c_i64, _c_i64, _vp, _c_int, _c_int, _c_int,
-                         _c_int, _c_int, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int, _c_i64,
-                         _vp],
+                         _c_int, _c_int, _vp, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_int,
+                         _c_i64, _vp],
     "erd_attn_fwd_bf16": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 4 + [_vp, _c_int, _c_float,
                                                                             _vp] + [_c_i64] * 4
                          + [_vp, _vp],
+    "erd_attn_fwd_sparse_bf16": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 4
+                                + [_vp, _c_int, _c_float, _vp] + [_c_i64] * 4
+                                + [_vp, _c_int, _vp, _c_i64, _vp, _vp, _vp],
+    "erd_gather_tokens": [_vp, _c_i64, _c_i64, _c_int, _vp, _c_i64, _c_i64, _vp, _c_int, _c_int,
+                          _c_int, _vp],
     "erd_attn_fp8_workspace_bytes": [_c_int, _c_int, _c_int, _c_int],
     "erd_attn_fwd_fp8": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 4 + [_vp, _c_int, _c_float,
                                                                            _vp] + [_c_i64] * 4

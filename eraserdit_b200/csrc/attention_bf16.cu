@@ -24,6 +24,16 @@
 // Tiles never straddle a segment; rows past a segment's end are masked (and
 // zero-filled by TMA past the slot).  Queries use the same tiling, and output
 // rows are scattered back with the caller's strides.
+//
+// The block-sparse instantiation (kSparse) replaces the mask-STA kernel
+// (layers/attention/backends/csrc/mask_sta/core.cu, driven by
+// layers/attention/backends/mask_sta.py:134-194).  Each CTA reads one schedule
+// row {query tile A, query tile B or -1, first entry, entries} and walks that
+// list of key tiles instead of all of them.  An entry is
+//   key tile | (64-token halves tile A attends) << 24 | (halves of B) << 26;
+// a softmax warpgroup masks the halves its tile does not attend (and writes
+// P = 0 for a key tile it skips entirely), so the two tiles of a CTA may have
+// different lists and the CTA computes their union.
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
@@ -62,7 +72,14 @@ struct AttnParams {
   __nv_bfloat16* out;
   long long o_rs, o_hs, o_bs, o_ss;
   int* status;
+  // block-sparse instantiation only
+  const int4* sched;         // per CTA: query tile A, query tile B (or -1), first entry, entries
+  const uint32_t* entries;   // key tile | A halves << 24 | B halves << 26
+  long long n_entries;
+  const int* out_rows;       // optional (one segment): output token of each query row
 };
+
+constexpr uint32_t kEntryTileMask = (1u << 24) - 1;
 
 struct __align__(8) AttnBarriers {
   uint64_t q_full;
@@ -92,6 +109,7 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_per_seg, int& se
   l0 = (tile - seg * tiles_per_seg) * kBlockN;
 }
 
+template <bool kSparse>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tmap_q,
                          const __grid_constant__ CUtensorMap tmap_k,
@@ -106,10 +124,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int pair = blockIdx.x;
   const int head = blockIdx.y;
   const int batch = blockIdx.z;
-  const int n_kv = p.q_tiles;  // the same tiling is used for keys and queries
+  // Query tiles of the two softmax warpgroups and the key tiles to visit: all
+  // of them (the same tiling is used for keys and queries), or a list.
+  int q_tile_a = 2 * static_cast<int>(blockIdx.x), q_tile_b = q_tile_a + 1;
+  int n_kv = p.q_tiles;
+  const uint32_t* list = nullptr;
+  if (kSparse) {
+    const int4 row = p.sched[blockIdx.x];
+    q_tile_a = row.x;
+    q_tile_b = row.y;
+    n_kv = row.w;
+    // A malformed row is skipped by the whole CTA (its outputs stay unwritten).
+    if (n_kv <= 0 || row.z < 0 || static_cast<long long>(row.z) + n_kv > p.n_entries ||
+        q_tile_a < 0 || q_tile_a >= p.q_tiles)
+      return;
+    list = p.entries + row.z;
+  }
   volatile int* abort = &bars->abort;
 
   if (threadIdx.x == 0) {
@@ -144,8 +176,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmap_q);
       tma_prefetch_desc(&tmap_k);
       tma_prefetch_desc(&tmap_v);
-      int qa = 2 * pair, qb = 2 * pair + 1;
-      if (qb >= p.q_tiles) qb = qa;
+      const int qa = q_tile_a;
+      const int qb = (q_tile_b < 0 || q_tile_b >= p.q_tiles) ? qa : q_tile_b;
       int seg, l0;
       const uint32_t qbar = smem_u32(&bars->q_full);
       mbar_arrive_expect_tx(qbar, 2 * kTileBytes);
@@ -156,7 +188,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < n_kv; ++j) {
         const int s = j % kStages;
         const uint32_t ph = (j / kStages) & 1;
-        tile_coords(j, p.tiles_per_seg, seg, l0);
+        // Key tiles past the last one read as zeros (TMA fills out-of-range
+        // boxes) and are masked by the softmax.
+        const int kv = kSparse ? static_cast<int>(__ldg(list + j) & kEntryTileMask) : j;
+        tile_coords(kv, p.tiles_per_seg, seg, l0);
         if (!mbar_wait(smem_u32(&bars->k_empty[s]), ph ^ 1, abort, p.status,
                        kStatusTimeoutProducer))
           break;
@@ -266,6 +301,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
+      // The list entry is read before the wait, which hides its latency.
+      const uint32_t entry = kSparse ? __ldg(list + j) : 0u;
       // Wait results are made warp-uniform: tcgen05.ld/st are .sync.aligned.
       if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->s_full[t]), j & 1, abort, p.status,
                                              kStatusTimeoutSoftmax))) {
@@ -273,18 +310,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      int seg, l0;
-      tile_coords(j, p.tiles_per_seg, seg, l0);
-      const int valid = min(kBlockN, p.seg_lens[seg] - l0);
+      // Columns [lo, hi) of this key tile are attended by this query tile.
+      int lo = 0, hi;
+      if (kSparse) {
+        const int kv = static_cast<int>(entry & kEntryTileMask);
+        const uint32_t halves = (entry >> (24 + 2 * t)) & 3u;
+        hi = 0;
+        if (halves != 0 && kv < p.q_tiles) {
+          int seg, l0;
+          tile_coords(kv, p.tiles_per_seg, seg, l0);
+          hi = min(kBlockN, p.seg_lens[seg] - l0);
+          if (!(halves & 2u)) hi = min(hi, kBlockN / 2);
+          if (!(halves & 1u)) lo = kBlockN / 2;
+        }
+      } else {
+        int seg, l0;
+        tile_coords(j, p.tiles_per_seg, seg, l0);
+        hi = min(kBlockN, p.seg_lens[seg] - l0);
+      }
       // Pass 1: row max over the whole S row (registers released afterwards).
+      // A key tile this query tile does not attend at all (sparse lists only)
+      // contributes P = 0 and leaves the running max and sum alone.
       float mx0 = -CUDART_INF_F, mx1 = -CUDART_INF_F, mx2 = -CUDART_INF_F, mx3 = -CUDART_INF_F;
-      {
+      if (!kSparse || hi > lo) {
         uint32_t sr[128];
         tmem_ld_wait_128(tS, sr);
-        if (valid < kBlockN) {
+        if (lo > 0 || hi < kBlockN) {
 #pragma unroll
           for (int i = 0; i < 128; ++i)
-            if (i >= valid) sr[i] = __float_as_uint(-CUDART_INF_F);
+            if (i < lo || i >= hi) sr[i] = __float_as_uint(-CUDART_INF_F);
         }
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
@@ -330,14 +384,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Pass 2: P = 2^(S c - m) in BF16, written to TMEM 64 S columns at a time.
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
+        uint32_t pk[32];
+        if (kSparse && (h * 64 >= hi || h * 64 + 64 <= lo)) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) pk[i] = 0u;
+          tmem_st32(tP + h * 32, pk);
+          continue;
+        }
         uint32_t sr[64];
         tmem_ld_wait_64(tS + h * 64, sr);
-        if (valid < kBlockN) {
+        if (lo > 0 || hi < kBlockN) {
 #pragma unroll
           for (int i = 0; i < 64; ++i)
-            if (h * 64 + i >= valid) sr[i] = __float_as_uint(-CUDART_INF_F);
+            if (h * 64 + i < lo || h * 64 + i >= hi) sr[i] = __float_as_uint(-CUDART_INF_F);
         }
-        uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           float x0, x1, p0, p1;
@@ -366,14 +426,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t oflat[64];
       tmem_ld_wait_64(tO, oflat);
       uint32_t(&o)[2][32] = *reinterpret_cast<uint32_t(*)[2][32]>(oflat);
-      const int qt = 2 * pair + t;
-      if (qt < p.q_tiles) {
+      const int qt = t == 0 ? q_tile_a : q_tile_b;
+      if (qt >= 0 && qt < p.q_tiles) {
         int seg, l0;
         tile_coords(qt, p.tiles_per_seg, seg, l0);
         const int tok = l0 + row;
         if (tok < p.seg_lens[seg]) {
           const float inv_l = 1.0f / l_run;
-          __nv_bfloat16* dst = p.out + seg * p.o_ss + batch * p.o_bs + head * p.o_hs + tok * p.o_rs;
+          const long long out_tok = (kSparse && p.out_rows != nullptr) ? __ldg(p.out_rows + tok) : tok;
+          __nv_bfloat16* dst =
+              p.out + seg * p.o_ss + batch * p.o_bs + head * p.o_hs + out_tok * p.o_rs;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
 #pragma unroll
@@ -432,20 +494,21 @@ bool strides_ok(int64_t a, int64_t b, int64_t c, int64_t d) {
   return a >= 0 && b >= 0 && c >= 0 && d >= 0 && ((a | b | c | d) & 7) == 0;
 }
 
-}  // namespace
+// Argument checks, tensor maps and parameters shared by the dense and the
+// block-sparse entry points.
+struct Launch {
+  CUtensorMap tq, tk, tv;
+  AttnParams p;
+};
 
-extern "C" int erd_attn_fwd_bf16(const void* q, const void* k, const void* v,
-                                 int64_t q_token_stride, int64_t q_head_stride,
-                                 int64_t q_batch_stride, int64_t q_seg_stride,
-                                 int64_t k_token_stride, int64_t k_head_stride,
-                                 int64_t k_batch_stride, int64_t k_seg_stride,
-                                 int64_t v_token_stride, int64_t v_head_stride,
-                                 int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads,
-                                 int seg_len, int nseg, const int32_t* seg_lens, int head_dim,
-                                 float softmax_scale,
-                                 void* out, int64_t o_token_stride, int64_t o_head_stride,
-                                 int64_t o_batch_stride, int64_t o_seg_stride, int* status,
-                                 void* stream) {
+int prepare(const void* q, const void* k, const void* v, int64_t q_token_stride,
+            int64_t q_head_stride, int64_t q_batch_stride, int64_t q_seg_stride,
+            int64_t k_token_stride, int64_t k_head_stride, int64_t k_batch_stride,
+            int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+            int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads, int seg_len,
+            int nseg, const int32_t* seg_lens, int head_dim, float softmax_scale, void* out,
+            int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride,
+            int64_t o_seg_stride, int* status, Launch* L) {
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr) return kErrNullPointer;
   if (head_dim != kHeadDim || batch <= 0 || heads <= 0 || seg_len <= 0 || nseg <= 0 ||
       nseg > kMaxSegments || batch > 65535 || heads > 65535)
@@ -464,18 +527,17 @@ extern "C" int erd_attn_fwd_bf16(const void* q, const void* k, const void* v,
 
   const int tiles_per_seg = (seg_len + kBlockN - 1) / kBlockN;
   const long long q_tiles = static_cast<long long>(tiles_per_seg) * nseg;
-  if (q_tiles > (1LL << 30)) return kErrTooLarge;
+  if (q_tiles > (1LL << 24)) return kErrTooLarge;
 
-  CUtensorMap tq, tk, tv;
-  if (make_operand_map(&tq, q, seg_len, heads, batch, nseg, q_token_stride, q_head_stride,
+  if (make_operand_map(&L->tq, q, seg_len, heads, batch, nseg, q_token_stride, q_head_stride,
                        q_batch_stride, q_seg_stride) ||
-      make_operand_map(&tk, k, seg_len, heads, batch, nseg, k_token_stride, k_head_stride,
+      make_operand_map(&L->tk, k, seg_len, heads, batch, nseg, k_token_stride, k_head_stride,
                        k_batch_stride, k_seg_stride) ||
-      make_operand_map(&tv, v, seg_len, heads, batch, nseg, v_token_stride, v_head_stride,
+      make_operand_map(&L->tv, v, seg_len, heads, batch, nseg, v_token_stride, v_head_stride,
                        v_batch_stride, v_seg_stride))
     return kErrTensorMap;
 
-  AttnParams p;
+  AttnParams& p = L->p;
   for (int s = 0; s < kMaxSegments; ++s)
     p.seg_lens[s] = (s < nseg) ? (seg_lens != nullptr ? seg_lens[s] : seg_len) : 0;
   p.seg_len = seg_len;
@@ -489,14 +551,75 @@ extern "C" int erd_attn_fwd_bf16(const void* q, const void* k, const void* v,
   p.o_bs = o_batch_stride;
   p.o_ss = o_seg_stride;
   p.status = status;
+  p.sched = nullptr;
+  p.entries = nullptr;
+  p.n_entries = 0;
+  p.out_rows = nullptr;
+  return kErrOk;
+}
 
-  cudaError_t e = cudaFuncSetAttribute(attn_fwd_bf16_kernel,
+template <bool kSparse>
+int launch(const Launch& L, unsigned ctas, int heads, int batch, void* stream) {
+  cudaError_t e = cudaFuncSetAttribute(attn_fwd_bf16_kernel<kSparse>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kSmemLaunchBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
-  const dim3 grid(static_cast<unsigned>((q_tiles + 1) / 2), static_cast<unsigned>(heads),
-                  static_cast<unsigned>(batch));
-  attn_fwd_bf16_kernel<<<grid, kThreads, kSmemLaunchBytes, static_cast<cudaStream_t>(stream)>>>(
-      tq, tk, tv, p);
+  const dim3 grid(ctas, static_cast<unsigned>(heads), static_cast<unsigned>(batch));
+  attn_fwd_bf16_kernel<kSparse><<<grid, kThreads, kSmemLaunchBytes,
+                                  static_cast<cudaStream_t>(stream)>>>(L.tq, L.tk, L.tv, L.p);
   return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+extern "C" int erd_attn_fwd_bf16(const void* q, const void* k, const void* v,
+                                 int64_t q_token_stride, int64_t q_head_stride,
+                                 int64_t q_batch_stride, int64_t q_seg_stride,
+                                 int64_t k_token_stride, int64_t k_head_stride,
+                                 int64_t k_batch_stride, int64_t k_seg_stride,
+                                 int64_t v_token_stride, int64_t v_head_stride,
+                                 int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads,
+                                 int seg_len, int nseg, const int32_t* seg_lens, int head_dim,
+                                 float softmax_scale,
+                                 void* out, int64_t o_token_stride, int64_t o_head_stride,
+                                 int64_t o_batch_stride, int64_t o_seg_stride, int* status,
+                                 void* stream) {
+  Launch L;
+  if (int rc = prepare(q, k, v, q_token_stride, q_head_stride, q_batch_stride, q_seg_stride,
+                       k_token_stride, k_head_stride, k_batch_stride, k_seg_stride,
+                       v_token_stride, v_head_stride, v_batch_stride, v_seg_stride, batch, heads,
+                       seg_len, nseg, seg_lens, head_dim, softmax_scale, out, o_token_stride,
+                       o_head_stride, o_batch_stride, o_seg_stride, status, &L))
+    return rc;
+  return launch<false>(L, static_cast<unsigned>((L.p.q_tiles + 1) / 2), heads, batch, stream);
+}
+
+extern "C" int erd_attn_fwd_sparse_bf16(
+    const void* q, const void* k, const void* v, int64_t q_token_stride, int64_t q_head_stride,
+    int64_t q_batch_stride, int64_t q_seg_stride, int64_t k_token_stride, int64_t k_head_stride,
+    int64_t k_batch_stride, int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+    int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads, int seg_len, int nseg,
+    const int32_t* seg_lens, int head_dim, float softmax_scale, void* out, int64_t o_token_stride,
+    int64_t o_head_stride, int64_t o_batch_stride, int64_t o_seg_stride, const int32_t* schedule,
+    int n_schedule, const uint32_t* entries, int64_t n_entries, const int32_t* out_rows,
+    int* status, void* stream) {
+  if (schedule == nullptr || entries == nullptr) return kErrNullPointer;
+  if (n_schedule <= 0 || n_schedule > (1 << 30) || n_entries <= 0) return kErrBadShape;
+  if ((reinterpret_cast<uintptr_t>(schedule) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(entries) & 3) != 0 ||
+      (reinterpret_cast<uintptr_t>(out_rows) & 3) != 0)
+    return kErrMisaligned;
+  if (out_rows != nullptr && nseg != 1) return kErrBadShape;
+  Launch L;
+  if (int rc = prepare(q, k, v, q_token_stride, q_head_stride, q_batch_stride, q_seg_stride,
+                       k_token_stride, k_head_stride, k_batch_stride, k_seg_stride,
+                       v_token_stride, v_head_stride, v_batch_stride, v_seg_stride, batch, heads,
+                       seg_len, nseg, seg_lens, head_dim, softmax_scale, out, o_token_stride,
+                       o_head_stride, o_batch_stride, o_seg_stride, status, &L))
+    return rc;
+  L.p.sched = reinterpret_cast<const int4*>(schedule);
+  L.p.entries = entries;
+  L.p.n_entries = n_entries;
+  L.p.out_rows = out_rows;
+  return launch<true>(L, static_cast<unsigned>(n_schedule), heads, batch, stream);
 }

@@ -38,6 +38,7 @@ struct PrologueParams {
   long long tab_ts, tab_bs;
   const float2* axis_tab;
   int nfreq, grid_f, grid_h, grid_w, token_offset;
+  const int* grid_index;  // optional: grid position of each token (tokens laid out in another order)
   __nv_bfloat16* q_out;
   __nv_bfloat16* k_out;
   __nv_bfloat16* v_out;
@@ -155,7 +156,8 @@ __global__ void __launch_bounds__(kTokensPerBlock * 32, 3)
 
   int pos_f = 0, pos_h = 0, pos_w = 0;
   if (kRopeMode == 2) {
-    const int gpos = p.token_offset + t;
+    const int gpos = p.grid_index != nullptr ? __ldg(p.grid_index + p.token_offset + t)
+                                             : p.token_offset + t;
     const int hw = p.grid_h * p.grid_w;
     pos_f = gpos / hw;
     const int rem = gpos - pos_f * hw;
@@ -282,7 +284,8 @@ extern "C" int erd_qk_norm_rope(const void* q_in, const void* k_in, const void* 
                                 float eps, int rope_mode, const float* cos_tab,
                                 const float* sin_tab, int64_t tab_token_stride,
                                 int64_t tab_batch_stride, const float* axis_table, int nfreq,
-                                int frames, int height, int width, int token_offset, void* q_out,
+                                int frames, int height, int width, int token_offset,
+                                const int32_t* grid_index, void* q_out,
                                 void* k_out, void* v_out, int64_t out_token_stride,
                                 int64_t out_batch_stride, int64_t out_head_stride,
                                 int heads_per_dest, int64_t out_dest_stride, void* stream) {
@@ -292,6 +295,7 @@ extern "C" int erd_qk_norm_rope(const void* q_in, const void* k_in, const void* 
       (kHidden / kHeadDimP) % heads_per_dest != 0)
     return kErrBadShape;
   if (rope_mode < 0 || rope_mode > 2) return kErrBadShape;
+  if (grid_index != nullptr && rope_mode != 2) return kErrBadShape;
   if (rope_mode == 1 && (cos_tab == nullptr || sin_tab == nullptr)) return kErrNullPointer;
   if (rope_mode == 2) {
     if (axis_table == nullptr) return kErrNullPointer;
@@ -333,6 +337,7 @@ extern "C" int erd_qk_norm_rope(const void* q_in, const void* k_in, const void* 
   p.grid_h = height;
   p.grid_w = width;
   p.token_offset = token_offset;
+  p.grid_index = grid_index;
   p.q_out = static_cast<__nv_bfloat16*>(q_out);
   p.k_out = static_cast<__nv_bfloat16*>(k_out);
   p.v_out = static_cast<__nv_bfloat16*>(v_out);

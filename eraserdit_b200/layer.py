@@ -14,6 +14,11 @@ output projection.  Data movement in HBM:
    ``precision="fp8"``, ``erd_attn_fwd_fp8`` quantises them into its
    workspace first);
 4. one cuBLAS GEMM applies ``to_out[0]``.
+
+With a block-sparse plan (``sparse=``, see ``mask_sta.SparsePlan``) the layer
+runs on a sequence in the plan's tile order: the prologue takes each token's
+RoPE coordinates from the plan's order, ``erd_attn_fwd_sparse_bf16`` replaces
+step 3, and the output stays in tile order (every other step is per token).
 """
 
 from __future__ import annotations
@@ -22,6 +27,7 @@ import torch
 import torch.nn.functional as F
 
 from .attention import attention_bshd
+from .mask_sta import sparse_attention_bshd
 from .operator_fusion import qk_norm_rope_into
 from .rotary import RopeAxisTable
 
@@ -71,26 +77,39 @@ class EraserDiTSelfAttention:
     def project_qkv(self, hidden_states: torch.Tensor) -> torch.Tensor:
         return F.linear(hidden_states, self.w_qkv, self.b_qkv)
 
-    def core(self, qkv: torch.Tensor, rope, out: torch.Tensor | None = None) -> torch.Tensor:
+    def core(self, qkv: torch.Tensor, rope, out: torch.Tensor | None = None,
+             sparse=None) -> torch.Tensor:
         """Prologue + attention on a [B, S, 3*2048] QKV buffer (modified in place)."""
         batch, seq, _ = qkv.shape
         q, k, v = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN], qkv[..., 2 * HIDDEN:]
+        if sparse is not None:
+            if self.precision != "bf16":
+                raise ValueError("the block-sparse path computes in BF16")
+            if isinstance(rope, RopeAxisTable) and rope.grid_index is None:
+                if sparse.order is None:
+                    raise ValueError("the sparse plan has no token order for the RoPE table")
+                rope = rope.in_order(sparse.order)
         qk_norm_rope_into(q, k, self.norm_q, self.norm_k, self.eps, rope, q, k)
         if out is None:
             out = torch.empty(batch, seq, HIDDEN, device=qkv.device, dtype=qkv.dtype)
-        attention_bshd(q.unflatten(2, (self.heads, HEAD_DIM)), k.unflatten(2, (self.heads, HEAD_DIM)),
-                       v.unflatten(2, (self.heads, HEAD_DIM)), self.softmax_scale,
-                       out=out.unflatten(2, (self.heads, HEAD_DIM)), precision=self.precision)
+        heads4 = lambda t: t.unflatten(2, (self.heads, HEAD_DIM))
+        if sparse is not None:
+            sparse_attention_bshd(heads4(q), heads4(k), heads4(v), self.softmax_scale, sparse,
+                                  out=heads4(out))
+        else:
+            attention_bshd(heads4(q), heads4(k), heads4(v), self.softmax_scale, out=heads4(out),
+                           precision=self.precision)
         return out
 
     def project_out(self, attn: torch.Tensor) -> torch.Tensor:
         return F.linear(attn, self.w_out, self.b_out)
 
-    def forward(self, hidden_states: torch.Tensor, rope: RopeAxisTable | tuple | None
-                ) -> torch.Tensor:
+    def forward(self, hidden_states: torch.Tensor, rope: RopeAxisTable | tuple | None,
+                sparse=None) -> torch.Tensor:
+        """``sparse``: a ``SparsePlan``; ``hidden_states`` are then in its tile order."""
         if hidden_states.dtype != torch.bfloat16 or hidden_states.shape[-1] != HIDDEN:
             raise ValueError("hidden_states must be BF16 [B, S, 2048]")
         qkv = self.project_qkv(hidden_states)
-        return self.project_out(self.core(qkv, rope))
+        return self.project_out(self.core(qkv, rope, sparse=sparse))
 
     __call__ = forward

@@ -91,9 +91,11 @@ def qk_norm_rope_into(query, key, q_weight, k_weight, eps, freqs, q_out, k_out,
     batch, tokens, hidden = query.shape
     out_token_stride = q_out.stride(1) if out_token_stride is None else out_token_stride
     out_batch_stride = q_out.stride(0) if out_batch_stride is None else out_batch_stride
+    grid_index = None
     if isinstance(freqs, RopeAxisTable):
         mode, cos, sin, tts, tbs = 2, None, None, 0, 0
         axis, nfreq, gf, gh, gw = freqs.table, freqs.nfreq, freqs.frames, freqs.height, freqs.width
+        grid_index = freqs.grid_index
     elif freqs is None:
         mode, cos, sin, tts, tbs = 0, None, None, 0, 0
         axis, nfreq, gf, gh, gw = None, 0, 0, 0, 0
@@ -108,7 +110,8 @@ def qk_norm_rope_into(query, key, q_weight, k_weight, eps, freqs, q_out, k_out,
             query.stride(1), query.stride(0), batch, tokens, hidden,
             _native.ptr(q_weight), _native.ptr(k_weight), float(eps), mode,
             _native.ptr(cos), _native.ptr(sin), tts, tbs, _native.ptr(axis), nfreq, gf, gh, gw,
-            int(token_offset), q_out.data_ptr(), k_out.data_ptr(), _native.ptr(v_out),
+            int(token_offset), _native.ptr(grid_index), q_out.data_ptr(), k_out.data_ptr(),
+            _native.ptr(v_out),
             out_token_stride, out_batch_stride, out_head_stride, heads_per_dest, out_dest_stride,
             _native.stream_handle(device))
     _native.check(rc, "erd_qk_norm_rope")

@@ -40,10 +40,20 @@ class RopeAxisTable:
     height: int
     width: int
     nfreq: int
+    # Optional device int32 [F*H*W]: grid position (f*H*W + h*W + w) of the
+    # token at each sequence position, when tokens are not in raster order.
+    grid_index: torch.Tensor | None = None
 
     @property
     def tokens(self) -> int:
         return self.frames * self.height * self.width
+
+    def in_order(self, grid_index: torch.Tensor) -> "RopeAxisTable":
+        """The same table for a sequence laid out in another token order."""
+        index = grid_index.to(device=self.table.device, dtype=torch.int32).contiguous()
+        if index.numel() != self.tokens:
+            raise ValueError("grid_index needs one entry per token")
+        return RopeAxisTable(self.table, self.frames, self.height, self.width, self.nfreq, index)
 
     def full(self, batch: int = 1, dim: int = 2048) -> tuple[torch.Tensor, torch.Tensor]:
         """Expand to the reference's [B, F*H*W, dim] cos/sin tables (for tests and
@@ -64,6 +74,9 @@ class RopeAxisTable:
         if pad:
             cos = torch.cat([torch.ones_like(cos[:, :pad]), cos], dim=-1)
             sin = torch.cat([torch.zeros_like(sin[:, :pad]), sin], dim=-1)
+        if self.grid_index is not None:
+            idx = self.grid_index.long().to(cos.device)
+            cos, sin = cos[idx], sin[idx]
         return (cos.unsqueeze(0).expand(batch, -1, -1).contiguous(),
                 sin.unsqueeze(0).expand(batch, -1, -1).contiguous())
 

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define ERD_ABI_VERSION 1
+#define ERD_ABI_VERSION 2
 
 /* ABI version probe; replaces eraserdit_mask_sta_abi()
  * (layers/attention/backends/csrc/mask_sta/core.cu:767). */
@@ -67,7 +67,10 @@ int erd_rope_axis_table(const float* freqs, int nfreq, int frames, int height, i
  * rope_mode 0: no RoPE; 1: full fp32 cos/sin tables indexed
  * [b * tab_batch_stride + t * tab_token_stride + c]; 2: per-axis table from
  * erd_rope_axis_table, token t of this call sitting at grid position
- * token_offset + t of a frames x height x width grid.
+ * token_offset + t of a frames x height x width grid, or, when grid_index
+ * (device int32, mode 2 only) is given, at grid_index[token_offset + t]
+ * (f * height * width + h * width + w): tokens laid out in another order,
+ * such as the tile order of the block-sparse attention.
  * Outputs: element (b, t, head h, d) goes to
  *   out + b*out_batch_stride + t*out_token_stride
  *       + (h % heads_per_dest)*out_head_stride + (h / heads_per_dest)*out_dest_stride + d.
@@ -78,7 +81,8 @@ int erd_qk_norm_rope(const void* q_in, const void* k_in, const void* v_in,
                      int hidden, const void* q_weight, const void* k_weight, float eps,
                      int rope_mode, const float* cos_tab, const float* sin_tab,
                      int64_t tab_token_stride, int64_t tab_batch_stride, const float* axis_table,
-                     int nfreq, int frames, int height, int width, int token_offset, void* q_out,
+                     int nfreq, int frames, int height, int width, int token_offset,
+                     const int32_t* grid_index, void* q_out,
                      void* k_out, void* v_out, int64_t out_token_stride, int64_t out_batch_stride,
                      int64_t out_head_stride, int heads_per_dest, int64_t out_dest_stride,
                      void* stream);
@@ -110,6 +114,48 @@ int erd_attn_fwd_bf16(const void* q, const void* k, const void* v, int64_t q_tok
                       float softmax_scale, void* out,
                       int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride,
                       int64_t o_seg_stride, int* status, void* stream);
+
+/*
+ * Block-sparse variant of erd_attn_fwd_bf16 for the mask-aware pattern.
+ * Replaces MaskSTA.__call__ (layers/attention/backends/mask_sta.py:160-194)
+ * and its kernel sta_mask_attention (csrc/mask_sta/core.cu); the pattern
+ * (mask_sta.py:66-105) arrives as per-CTA work lists instead of the
+ * reference's per-query-block LUT:
+ *   schedule  device int32 [n_schedule][4], 16-byte aligned: query tile A,
+ *             query tile B (or -1), first entry, number of entries (>= 1);
+ *   entries   device uint32 [n_entries]: key tile | (64-token halves of the
+ *             key tile that A attends, bit 0 = first half) << 24 | (halves B
+ *             attends) << 26.
+ * Tiles are the 128-token tiles of the segmented layout (segment s, local
+ * tile i -> s * ceil(seg_len / 128) + i).  Every query tile to be written
+ * appears in exactly one schedule row, with at least one attended half.
+ * out_rows (device int32 [seg_len], nseg == 1 only, may be NULL) gives the
+ * output token of each query token: the output is scattered back from the
+ * tile order the inputs are laid out in.
+ * All other arguments and the result are those of erd_attn_fwd_bf16.
+ */
+int erd_attn_fwd_sparse_bf16(
+    const void* q, const void* k, const void* v, int64_t q_token_stride, int64_t q_head_stride,
+    int64_t q_batch_stride, int64_t q_seg_stride, int64_t k_token_stride, int64_t k_head_stride,
+    int64_t k_batch_stride, int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+    int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads, int seg_len, int nseg,
+    const int32_t* seg_lens, int head_dim, float softmax_scale, void* out, int64_t o_token_stride,
+    int64_t o_head_stride, int64_t o_batch_stride, int64_t o_seg_stride, const int32_t* schedule,
+    int n_schedule, const uint32_t* entries, int64_t n_entries, const int32_t* out_rows,
+    int* status, void* stream);
+
+/*
+ * Token gather: dst[b][t][:] = src[b][index[t]][:] for rows of row_elems
+ * BF16 values (a multiple of 8), index a device int32 [tokens] with entries
+ * in [0, src_tokens).  Lays Q/K/V out in the tile order of the block-sparse
+ * pattern, replacing the row_order gathers of the reference's quantisation
+ * kernels (layers/attention/backends/mask_sta.py:28-63) and V preparation
+ * (sta_mask_prepare_v).  Strides in elements, multiples of 8.
+ */
+int erd_gather_tokens(const void* src, int64_t src_token_stride, int64_t src_batch_stride,
+                      int src_tokens, void* dst, int64_t dst_token_stride,
+                      int64_t dst_batch_stride, const int32_t* index, int batch, int tokens,
+                      int row_elems, void* stream);
 
 /*
  * SageAttention-style FP8 attention, head_dim 64: K smoothed by its per-head
