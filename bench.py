@@ -8,6 +8,13 @@ hidden states, N(0, 0.02) weights, seed 1).  ``value`` is whole-job TFLOP/s
 (19.645 TFLOP per layer / max-over-ranks step time).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+                    [--fp8 | --sparse] [--cfg C]
+
+``--fp8`` times the Sage-style FP8 attention (configuration 3's numerics);
+``--sparse`` the mask-aware block-sparse attention of configuration 4 (tokens
+in tile order, a seeded ellipse mask per latent frame): its ``value`` counts
+the FLOPs of the kept (query, key) pairs, ``dense_equivalent`` the full
+layer's FLOPs over the same time.
 """
 
 from __future__ import annotations
@@ -200,18 +207,39 @@ def build_problem(device, precision: str = "bf16"):
     return layer, rope
 
 
+SPARSE_WORKLOAD = ("config 4: mask-aware block-sparse self-attention layer, B=2 x 32640 tokens "
+                   "(16x34x60) in 4x2x4-cell tile order, one seeded ellipse per latent frame "
+                   "(semi-axes 6-12 cells, drift <= 1 cell/frame, seed 3) dilated by 2 cells; "
+                   "masked-neighbourhood query blocks attend all keys, the others a 3x9x9-cell "
+                   "window rounded out to tiles; BF16")
+
+
+def build_sparse_plan(device):
+    """Configuration 4's pattern; returns (plan, kept fraction, issued fraction)."""
+    from eraserdit_b200 import sparse_pattern as sp
+    from eraserdit_b200.mask_sta import SparsePlan
+    geom = sp.CONFIG4_GEOMETRY
+    plan = SparsePlan.from_mask(sp.ellipse_masks(geom.grid, seed=3), geom, device)
+    issued = plan.host.issued_pairs / plan.host.dense_pairs
+    return plan, plan.keep_fraction, issued
+
+
 def run_single(args) -> None:
     from eraserdit_b200 import _native
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
     precision = "fp8" if args.fp8 else "bf16"
     layer, rope = build_problem(device, precision)
+    plan, kept, issued = build_sparse_plan(device) if args.sparse else (None, 1.0, 1.0)
+    if plan is not None:
+        rope = rope.in_order(plan.order)  # the sequence is laid out in tile order
     g = torch.Generator(device=device).manual_seed(1)
     x = torch.randn(BATCH, SEQ, HIDDEN, generator=g, device=device).bfloat16()
     stream = torch.cuda.current_stream(device)
     attn_events = []
 
     from eraserdit_b200.attention import attention_bshd
+    from eraserdit_b200.mask_sta import sparse_attention_bshd
     from eraserdit_b200.operator_fusion import qk_norm_rope_into
     attn_out = torch.empty(BATCH, SEQ, HIDDEN, device=device, dtype=torch.bfloat16)
 
@@ -224,9 +252,13 @@ def run_single(args) -> None:
         if record:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-        attention_bshd(q.unflatten(2, (HEADS, HEAD_DIM)), k.unflatten(2, (HEADS, HEAD_DIM)),
-                       v.unflatten(2, (HEADS, HEAD_DIM)), layer.softmax_scale,
-                       out=attn_out.unflatten(2, (HEADS, HEAD_DIM)), precision=precision)
+        heads4 = lambda t: t.unflatten(2, (HEADS, HEAD_DIM))
+        if plan is not None:
+            sparse_attention_bshd(heads4(q), heads4(k), heads4(v), layer.softmax_scale, plan,
+                                  out=heads4(attn_out))
+        else:
+            attention_bshd(heads4(q), heads4(k), heads4(v), layer.softmax_scale,
+                           out=heads4(attn_out), precision=precision)
         if record:
             e1.record(stream)
             attn_events.append((e0, e1))
@@ -253,12 +285,14 @@ def run_single(args) -> None:
     host_x = x.cpu().pin_memory()
     host_y = torch.empty(BATCH, SEQ, HIDDEN, dtype=torch.bfloat16).pin_memory()
     for _ in range(max(args.warmup, 1)):
-        host_y.copy_(layer(host_x.to(device, non_blocking=True), rope), non_blocking=True)
+        host_y.copy_(layer(host_x.to(device, non_blocking=True), rope, sparse=plan),
+                     non_blocking=True)
     torch.cuda.synchronize()
     e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
     for _ in range(args.steps):
-        host_y.copy_(layer(host_x.to(device, non_blocking=True), rope), non_blocking=True)
+        host_y.copy_(layer(host_x.to(device, non_blocking=True), rope, sparse=plan),
+                     non_blocking=True)
     e_stop.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e_start.elapsed_time(e_stop) / args.steps
@@ -269,31 +303,45 @@ def run_single(args) -> None:
     peak = peaks[peak_key]
     if args.fp8:  # dense FP8 runs at twice the BF16 rate on this part
         peak, peak_key = 2 * peak, f"2 x {peak_key} (dense fp8 = 2x bf16)"
-    achieved = ATTN_FLOP / (core_ms / 1e3) / 1e12
+    # Sparse: algorithmic FLOPs are those of the kept pairs; the kernel's
+    # roofline counts the products it issues (the union of a CTA's two lists).
+    layer_flop = LINEAR_FLOP + ATTN_FLOP * kept
+    achieved = ATTN_FLOP * issued / (core_ms / 1e3) / 1e12
     clock = clocks.summary()
+    if plan is not None:
+        workload, kernel = SPARSE_WORKLOAD, "attn_fwd_bf16 (block-sparse instantiation)"
+    elif args.fp8:
+        workload = WORKLOAD + ", FP8 attention (configuration 3 numerics)"
+        kernel = "attn_fwd_fp8 (+ fp8 quantize)"
+    else:
+        workload, kernel = WORKLOAD, "attn_fwd_bf16"
     line = {
-        "metric": METRIC, "value": LAYER_FLOP / (ms / 1e3) / 1e12, "unit": UNIT, "n_gpus": 1,
+        "metric": METRIC, "value": layer_flop / (ms / 1e3) / 1e12, "unit": UNIT, "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "e4m3/bf16" if args.fp8 else "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD + (", FP8 attention (configuration 3 numerics)"
-                                           if args.fp8 else ""),
+        "config": {"workload": workload,
                    "global_batch": BATCH, "seq_len": SEQ, "parallelism": "sp1",
                    "l2": "inputs larger than L2 (x 267 MB, QKV 802 MB per step)"},
-        "layer_tflop": LAYER_FLOP / 1e12,
-        "roofline": {"kernel": "attn_fwd_fp8 (+ fp8 quantize)" if args.fp8 else "attn_fwd_bf16",
+        "layer_tflop": layer_flop / 1e12,
+        "roofline": {"kernel": kernel,
                      "bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT,
                      "frac": achieved / peak,
                      "peak_source": f"{peak_src} {peak_key}",
-                     "traffic": profiled_traffic("attn_fwd_bf16_config1"),
+                     "traffic": None if (args.fp8 or plan is not None)
+                     else profiled_traffic("attn_fwd_bf16_config1"),
                      "kernel_ms": core_ms},
-        "e2e": {"value": LAYER_FLOP / (e2e_ms / 1e3) / 1e12, "unit": UNIT,
+        "e2e": {"value": layer_flop / (e2e_ms / 1e3) / 1e12, "unit": UNIT,
                 "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": host_x.numel() * host_x.element_size(),
                 "d2h_bytes_per_step": host_y.numel() * host_y.element_size()},
         "gpu_launches": (4 if args.fp8 else 2) * args.steps,
         "clocks": clock,
     }
+    if plan is not None:
+        line["sparsity"] = {"kept_pair_fraction": kept, "issued_pair_fraction": issued,
+                            "dense_equivalent": LAYER_FLOP / (ms / 1e3) / 1e12,
+                            "dense_equivalent_e2e": LAYER_FLOP / (e2e_ms / 1e3) / 1e12}
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     print(json.dumps(line), flush=True)
@@ -309,7 +357,11 @@ def main() -> None:
     parser.add_argument("--cfg", type=int, default=1, help="CFG branches on separate rank groups")
     parser.add_argument("--fp8", action="store_true",
                         help="Sage-style FP8 attention (configuration 3) instead of BF16")
+    parser.add_argument("--sparse", action="store_true",
+                        help="mask-aware block-sparse attention (configuration 4)")
     args = parser.parse_args()
+    if args.fp8 and args.sparse:
+        parser.error("--fp8 and --sparse are separate configurations")
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)

@@ -38,12 +38,13 @@ def run_sequence_parallel(args) -> None:
         group, ranks, index = groups.get("ulysses") if world // cfg > 1 else (None, (rank,), 0)
         cfg_index = topo.coordinates(rank)[3]
         layer, rope = B.build_problem(device, "fp8" if args.fp8 else "bf16")
+        plan, kept, issued = B.build_sparse_plan(device) if args.sparse else (None, 1.0, 1.0)
         g = torch.Generator(device=device).manual_seed(1)
         x_full = torch.randn(B.BATCH, B.SEQ, B.HIDDEN, generator=g, device=device).bfloat16()
         per_branch = B.BATCH // cfg
         x_branch = x_full[cfg_index * per_branch:(cfg_index + 1) * per_branch]
         sp = UlyssesSelfAttention(layer, len(ranks), index, peer_exchange(group, ranks, index),
-                                  group_ranks=ranks)
+                                  group_ranks=ranks, sparse=plan)
         x_local = x_branch[:, sp.partition(B.SEQ)].contiguous()
         del x_full
         stream = torch.cuda.current_stream(device)
@@ -105,30 +106,40 @@ def run_sequence_parallel(args) -> None:
             peak = peaks[peak_key]
             if args.fp8:
                 peak, peak_key = 2 * peak, f"2 x {peak_key} (dense fp8 = 2x bf16)"
-            local_attn_flop = B.ATTN_FLOP / world
+            local_attn_flop = B.ATTN_FLOP * issued / world
             achieved = local_attn_flop / (kernel_ms / 1e3) / 1e12
+            layer_flop = B.LINEAR_FLOP + B.ATTN_FLOP * kept
             parallelism = f"cfg{cfg}xsp{world // cfg}" if cfg > 1 else f"sp{world}"
-            print(json.dumps({
-                "metric": B.METRIC, "value": B.LAYER_FLOP / (ms / 1e3) / 1e12, "unit": B.UNIT,
+            if plan is not None:
+                workload = B.SPARSE_WORKLOAD + ", Ulysses SP (whole 128-token blocks per rank)"
+                kernel = "attn_fwd_bf16 (block-sparse instantiation)"
+            else:
+                workload = B.WORKLOAD.replace("config 1", "config 2 (Ulysses SP)")
+                kernel = "attn_fwd_fp8" if args.fp8 else "attn_fwd_bf16"
+            line = {
+                "metric": B.METRIC, "value": layer_flop / (ms / 1e3) / 1e12, "unit": B.UNIT,
                 "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "e4m3/bf16" if args.fp8 else "bf16", "data": "synthetic",
-                "config": {"workload": B.WORKLOAD.replace("config 1", "config 2 (Ulysses SP)"),
+                "config": {"workload": workload,
                            "global_batch": B.BATCH, "seq_len": B.SEQ, "parallelism": parallelism,
                            "l2": "inputs larger than L2"},
-                "layer_tflop": B.LAYER_FLOP / 1e12,
-                "roofline": {"kernel": ("attn_fwd_fp8" if args.fp8 else "attn_fwd_bf16")
-                             + " (per rank, max over ranks)",
+                "layer_tflop": layer_flop / 1e12,
+                "roofline": {"kernel": kernel + " (per rank, max over ranks)",
                              "bound": "tensor", "achieved": achieved, "peak": peak,
                              "unit": B.UNIT, "frac": achieved / peak,
                              "peak_source": f"{src} {peak_key}",
                              "traffic": None, "kernel_ms": kernel_ms},
-                "e2e": {"value": B.LAYER_FLOP / (e2e_ms / 1e3) / 1e12, "unit": B.UNIT,
+                "e2e": {"value": layer_flop / (e2e_ms / 1e3) / 1e12, "unit": B.UNIT,
                         "ms_per_step": e2e_ms,
                         "h2d_bytes_per_step": host_x.numel() * host_x.element_size() * world,
                         "d2h_bytes_per_step": host_y.numel() * host_y.element_size() * world},
                 "gpu_launches": (4 if args.fp8 else 2) * args.steps,
                 "clocks": clock,
-            }), flush=True)
+            }
+            if plan is not None:
+                line["sparsity"] = {"kept_pair_fraction": kept, "issued_pair_fraction": issued,
+                                    "dense_equivalent": B.LAYER_FLOP / (ms / 1e3) / 1e12}
+            print(json.dumps(line), flush=True)
     finally:
         dist.destroy_process_group()

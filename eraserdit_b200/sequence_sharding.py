@@ -23,6 +23,20 @@ def floor_lengths(length: int, degree: int) -> list[int]:
     return [length * (r + 1) // degree - length * r // degree for r in range(degree)]
 
 
+def block_bounds(length: int, degree: int, rank: int, block: int = 128) -> tuple[int, int]:
+    """Token range of ``rank`` when whole ``block``-token blocks are floor
+    partitioned (the block-sparse attention needs every source segment to hold
+    whole query / key tiles)."""
+    if length % block:
+        raise ValueError(f"block partition needs a multiple of {block} tokens")
+    b0, b1 = floor_bounds(length // block, degree, rank)
+    return b0 * block, b1 * block
+
+
+def block_lengths(length: int, degree: int, block: int = 128) -> list[int]:
+    return [n * block for n in floor_lengths(length // block, degree)]
+
+
 @dataclass(frozen=True)
 class SequenceShardPlan:
     """One rank's equal-size slice of a right-padded sequence."""

@@ -28,6 +28,11 @@ floor-partitioned token range of the sequence (``mesh.py:163-169``) and all
 
 The two collectives are the only data-path communication; with CFG the
 Ulysses group is one branch's ranks (``eraserdit_b200.topology``).
+
+With a block-sparse plan (``sparse=``) the sequence is in the plan's tile
+order, ranks own whole 128-token blocks (a floor partition of the blocks), and
+step 4 runs ``erd_attn_fwd_sparse_bf16`` with the plan's lists translated to
+the received segments.
 """
 
 from __future__ import annotations
@@ -42,7 +47,8 @@ import torch.nn.functional as F
 from . import _native
 from .layer import HEAD_DIM, HIDDEN, EraserDiTSelfAttention
 from .operator_fusion import qk_norm_rope_into
-from .sequence_sharding import floor_bounds, floor_lengths
+from .rotary import RopeAxisTable
+from .sequence_sharding import block_bounds, block_lengths, floor_bounds, floor_lengths
 
 FLAG = 8  # elements reserved at the head of every returned chunk (16 bytes)
 
@@ -95,7 +101,8 @@ class UlyssesSelfAttention:
     """One self-attention layer with Ulysses sequence parallelism on ``degree`` ranks."""
 
     def __init__(self, layer: EraserDiTSelfAttention, degree: int, rank: int,
-                 exchange: Exchange, group_ranks: tuple[int, ...] | None = None) -> None:
+                 exchange: Exchange, group_ranks: tuple[int, ...] | None = None,
+                 sparse=None) -> None:
         if layer.heads % degree:
             raise ValueError("attention heads must be divisible by Ulysses degree")
         if degree > 16:
@@ -108,12 +115,26 @@ class UlyssesSelfAttention:
         self.local_heads = layer.heads // degree
         self._buffers: dict[tuple, tuple] = {}
         self.calls = 0
+        if sparse is not None and layer.precision != "bf16":
+            raise ValueError("the block-sparse path computes in BF16")
+        self.sparse = sparse
+        self._sparse_segments: dict[int, object] = {}
+
+    def _bounds(self, length: int, rank: int) -> tuple[int, int]:
+        if self.sparse is not None:
+            return block_bounds(length, self.degree, rank)
+        return floor_bounds(length, self.degree, rank)
+
+    def _lengths(self, length: int) -> list[int]:
+        if self.sparse is not None:
+            return block_lengths(length, self.degree)
+        return floor_lengths(length, self.degree)
 
     # ------------------------------------------------------------ partition
     def partition(self, length: int) -> slice:
         if length < self.degree:
             raise ValueError("sequence length must be at least SP degree")
-        start, end = floor_bounds(length, self.degree, self.rank)
+        start, end = self._bounds(length, self.rank)
         return slice(start, end)
 
     def _buffers_for(self, batch: int, length: int, device, dtype):
@@ -121,7 +142,7 @@ class UlyssesSelfAttention:
         cached = self._buffers.get(key)
         if cached is None:
             n, hl = self.degree, self.local_heads
-            lengths = floor_lengths(length, n)
+            lengths = self._lengths(length)
             lmax, lme = max(lengths), lengths[self.rank]
             row1 = 3 * batch * hl * HEAD_DIM
             row2 = batch * hl * HEAD_DIM
@@ -140,9 +161,12 @@ class UlyssesSelfAttention:
         batch = x_local.shape[0]
         lengths, send1, recv1, send2, recv2, row1, _ = self._buffers_for(
             batch, length, x_local.device, x_local.dtype)
-        start, end = floor_bounds(length, self.degree, self.rank)
+        start, end = self._bounds(length, self.rank)
         if x_local.shape[1] != end - start:
-            raise ValueError("local sequence length must match the floor partition")
+            raise ValueError("local sequence length must match the rank's partition")
+        if (self.sparse is not None and isinstance(rope, RopeAxisTable)
+                and rope.grid_index is None):
+            rope = rope.in_order(self.sparse.order)
         qkv = self.layer.project_qkv(x_local)
         q, k, v = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN], qkv[..., 2 * HIDDEN:]
         hl = self.local_heads
@@ -182,6 +206,17 @@ class UlyssesSelfAttention:
         o = step.send2.view(-1)[FLAG:]
         strides = (row1, HEAD_DIM, hl * HEAD_DIM, lmax * row1)  # token, head, batch, segment
         o_strides = (b * hl * HEAD_DIM, HEAD_DIM, hl * HEAD_DIM, FLAG + lmax * b * hl * HEAD_DIM)
+        if self.sparse is not None:
+            from .mask_sta import sparse_attention_into
+            plan = self._sparse_segments.get(step.length)
+            if plan is None:
+                plan = self.sparse.for_segments([l // 128 for l in step.lengths], lmax // 128)
+                self._sparse_segments[step.length] = plan
+            sparse_attention_into(r, r[chunk:], r[2 * chunk:], o, self.layer.softmax_scale, plan,
+                                  batch=b, heads=hl, seg_len=lmax, nseg=n, seg_lens=step.lengths,
+                                  q_strides=strides, k_strides=strides, v_strides=strides,
+                                  o_strides=o_strides)
+            return
         fp8 = self.layer.precision == "fp8"
         extra = fp8_workspace(r.device, b, hl, lmax, n) if fp8 else ()
         _segmented_call("erd_attn_fwd_fp8" if fp8 else "erd_attn_fwd_bf16", r, r[chunk:],
@@ -229,14 +264,15 @@ class UlyssesSelfAttention:
     __call__ = forward
 
 
-def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, rope
-                  ) -> list[torch.Tensor]:
+def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, rope,
+                  sparse=None) -> list[torch.Tensor]:
     """Run all ``degree`` ranks of the Ulysses layer inside one process on one
     device, exchanging chunks by copies (the same buffers and kernels as the
     NCCL path).  Returns each rank's output; used to check the data layout on
     a single GPU."""
     length = x.shape[1]
-    ranks = [UlyssesSelfAttention(layer, degree, r, exchange=None) for r in range(degree)]
+    ranks = [UlyssesSelfAttention(layer, degree, r, exchange=None, sparse=sparse)
+             for r in range(degree)]
     steps = []
     for r in ranks:
         sl = r.partition(length)

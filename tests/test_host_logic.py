@@ -38,3 +38,14 @@ def test_plan_validation_errors():
         plan_sequence_shards(10.0, 2, 0)
     with pytest.raises(ValueError):
         DiTTopology(cfg=3)
+
+
+def test_block_partition():
+    from eraserdit_b200.sequence_sharding import block_bounds, block_lengths
+    assert block_lengths(32640, 8) == [3968] + [4096] * 7
+    bounds = [block_bounds(32640, 8, r) for r in range(8)]
+    assert bounds[0][0] == 0 and bounds[-1][1] == 32640
+    assert all(a[1] == b[0] for a, b in zip(bounds, bounds[1:]))
+    assert all((e - s) % 128 == 0 for s, e in bounds)
+    with pytest.raises(ValueError):
+        block_bounds(1000, 2, 0)

@@ -180,3 +180,27 @@ def test_config4_layer_against_fp32():
     assert torch.isfinite(got).all()
     assert max_abs(got, want) <= MAX_ABS
     assert cosine(got, want) >= MIN_COSINE
+
+
+@pytest.mark.parametrize("degree", [2, 8])
+def test_sparse_ulysses_emulated(degree):
+    """Configuration 4 at SP2 / SP8 (all ranks in one process, same buffers and
+    kernels as the NCCL path) against the single-GPU sparse layer."""
+    from eraserdit_b200.layer import EraserDiTSelfAttention
+    from eraserdit_b200.mask_sta import SparsePlan
+    from eraserdit_b200.rotary import LTXVideoRotaryPosEmbed
+    from eraserdit_b200.synthetic import make_params
+    from eraserdit_b200.ulysses import emulate_ranks
+    geom = sp.CONFIG4_GEOMETRY
+    plan = SparsePlan.from_mask(sp.ellipse_masks(geom.grid, seed=3), geom, "cuda")
+    p = make_params(1, 1e-6, device="cuda")
+    layer = EraserDiTSelfAttention.from_params(p.to(torch.bfloat16), device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x = torch.randn(2, geom.tokens, 2048, generator=g, device="cuda").bfloat16()
+    rope = LTXVideoRotaryPosEmbed()(*geom.grid)
+    one = layer(x, rope, sparse=plan)
+    parts = emulate_ranks(layer, degree, x, rope, sparse=plan)
+    assert [t.shape[1] % 128 for t in parts] == [0] * degree  # whole blocks per rank
+    got = torch.cat(parts, dim=1)
+    assert max_abs(got, one) <= 1e-2
+    assert cosine(got, one) >= 0.99999
