@@ -75,18 +75,59 @@ def profiled_traffic(kernel: str) -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled during the timed region.
+
+    Reads NVML from a thread every 5 ms (read-only queries); falls back to
+    ``nvidia-smi -lms 50`` when NVML is unavailable.  Nothing is changed on the
+    device."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index: int) -> None:
+    def __init__(self, index: int, interval: float = 0.005) -> None:
         self.index = index
+        self.interval = interval
         self.proc = None
         self.file = None
+        self.thread = None
+        self.samples: list[tuple[float, int]] = []
+        self.max_sm = None
+
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        try:  # the CUDA ordinal and the NVML index differ under CUDA_VISIBLE_DEVICES
+            prop = torch.cuda.get_device_properties(self.index)
+            bus = f"{prop.pci_domain_id:08X}:{prop.pci_bus_id:02X}:{prop.pci_device_id:02X}.0"
+            return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
 
     def __enter__(self):
+        import threading
+        try:
+            nvml, handle = self._nvml_handle()
+            self.max_sm = nvml.nvmlDeviceGetMaxClockInfo(handle, nvml.NVML_CLOCK_SM)
+            self._stop = threading.Event()
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        sm = nvml.nvmlDeviceGetClockInfo(handle, nvml.NVML_CLOCK_SM)
+                        bits = nvml.nvmlDeviceGetCurrentClocksThrottleReasons(handle)
+                        self.samples.append((float(sm), int(bits)))
+                    except Exception:
+                        pass
+                    self._stop.wait(self.interval)
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.thread = None
         try:
             self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(
@@ -97,6 +138,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -106,6 +150,13 @@ class ClockSampler:
         return False
 
     def summary(self) -> dict:
+        if self.thread is not None:
+            sm = [c for c, _ in self.samples]
+            reasons = sorted({name for _, bits in self.samples
+                              for bit, name in self.REASONS.items() if bits & bit})
+            return {"sm_mhz": statistics.median(sm) if sm else None,
+                    "sm_max_mhz": float(self.max_sm) if self.max_sm else None,
+                    "reasons": reasons, "samples": len(sm), "source": "nvml 5 ms"}
         if self.proc is None or self.file is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.file.flush()
@@ -124,7 +175,7 @@ class ClockSampler:
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi 50 ms"}
 
 
 # ------------------------------------------------------------- CPU sample

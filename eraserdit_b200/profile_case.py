@@ -2,6 +2,11 @@
 
     python -m eraserdit_b200.profile_case attention --batch 1 --seq 16320 --iters 3
     python -m eraserdit_b200.profile_case prologue --batch 2 --seq 32640 --iters 3
+    python -m eraserdit_b200.profile_case fp8 --batch 1 --seq 16320 --iters 3
+    python -m eraserdit_b200.profile_case sparse --batch 1 --heads 16 --iters 3
+
+``sparse`` runs the configuration-4 pattern (32640 tokens in tile order, the
+seeded ellipse mask) whatever ``--seq`` says.
 
 Each runs the named kernel ``iters`` times on seeded inputs (sized above L2 by
 default) and exits 0, so that an ncu capture (``-k``/``-c``) of one to three
@@ -17,7 +22,7 @@ import torch
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["attention", "prologue"])
+    ap.add_argument("kernel", choices=["attention", "prologue", "fp8", "sparse"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seq", type=int, default=16320)
     ap.add_argument("--heads", type=int, default=32)
@@ -27,14 +32,26 @@ def main() -> None:
     torch.cuda.set_device(device)
     g = torch.Generator(device=device).manual_seed(0)
     from eraserdit_b200 import _native
-    if args.kernel == "attention":
+    if args.kernel in ("attention", "fp8", "sparse"):
         from eraserdit_b200.attention import attention_bshd
+        plan = None
+        if args.kernel == "sparse":
+            from eraserdit_b200 import sparse_pattern as sp
+            from eraserdit_b200.mask_sta import SparsePlan, sparse_attention_bshd
+            geom = sp.CONFIG4_GEOMETRY
+            plan = SparsePlan.from_mask(sp.ellipse_masks(geom.grid, seed=3), geom, device)
+            args.seq = geom.tokens
         qkv = torch.randn(args.batch, args.seq, 3, args.heads, 64, generator=g,
                           device=device).bfloat16()
         out = torch.empty(args.batch, args.seq, args.heads, 64, device=device,
                           dtype=torch.bfloat16)
+        q, k, v = qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2]
         for _ in range(args.iters):
-            attention_bshd(qkv[:, :, 0], qkv[:, :, 1], qkv[:, :, 2], 0.125, out=out)
+            if plan is not None:
+                sparse_attention_bshd(q, k, v, 0.125, plan, out=out)
+            else:
+                attention_bshd(q, k, v, 0.125, out=out,
+                               precision="fp8" if args.kernel == "fp8" else "bf16")
     else:
         from eraserdit_b200.operator_fusion import qk_norm_rope_into
         from eraserdit_b200.rotary import LTXVideoRotaryPosEmbed
