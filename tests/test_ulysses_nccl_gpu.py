@@ -1,5 +1,6 @@
 """Ulysses SP over real NCCL on every visible GPU (skipped with fewer than 2):
-each rank's output equals the single-GPU layer's rows for its tokens."""
+each rank's output equals the single-GPU layer's rows for its tokens, dense
+and block-sparse."""
 import os
 import socket
 import tempfile
@@ -46,6 +47,24 @@ def _rank(rank, world, port, out_dir):
             cos = float(torch.nn.functional.cosine_similarity(
                 got.float().flatten(), want[:, sl].float().flatten(), dim=0))
             assert err <= 1e-2 and cos >= 0.99999, (err, cos)
+        # block-sparse attention over the exchange (whole 128-token blocks per rank)
+        from eraserdit_b200 import sparse_pattern as sp_pattern
+        from eraserdit_b200.mask_sta import SparsePlan
+        geom = sp_pattern.StaGeometry(grid=(8, 16, 32), window=(1, 3, 2), kv_block=128)
+        plan = SparsePlan.from_mask(
+            sp_pattern.ellipse_masks(geom.grid, seed=4, semi_axes=(2, 4)), geom, device)
+        rope = LTXVideoRotaryPosEmbed()(*geom.grid, device=device)
+        g = torch.Generator(device=device).manual_seed(5)
+        x = torch.randn(2, geom.tokens, 2048, generator=g, device=device).bfloat16()
+        want = layer(x, rope, sparse=plan)
+        sp = UlyssesSelfAttention(layer, world, index, peer_exchange(group, ranks, index), ranks,
+                                  sparse=plan)
+        sl = sp.partition(x.shape[1])
+        got = sp(x[:, sl].contiguous(), rope, x.shape[1])
+        err = float((got.float() - want[:, sl].float()).abs().max())
+        cos = float(torch.nn.functional.cosine_similarity(
+            got.float().flatten(), want[:, sl].float().flatten(), dim=0))
+        assert err <= 1e-2 and cos >= 0.99999, ("sparse", err, cos)
         torch.cuda.synchronize()
         open(os.path.join(out_dir, f"ok{rank}"), "w").close()
     finally:
