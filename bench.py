@@ -410,6 +410,8 @@ def main() -> None:
                         help="Sage-style FP8 attention (configuration 3) instead of BF16")
     parser.add_argument("--sparse", action="store_true",
                         help="mask-aware block-sparse attention (configuration 4)")
+    parser.add_argument("--head-chunks", type=int, default=None,
+                        help="Ulysses head chunks (exchange/attention overlap); default: policy")
     args = parser.parse_args()
     if args.fp8 and args.sparse:
         parser.error("--fp8 and --sparse are separate configurations")

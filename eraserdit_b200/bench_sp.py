@@ -44,24 +44,20 @@ def run_sequence_parallel(args) -> None:
         per_branch = B.BATCH // cfg
         x_branch = x_full[cfg_index * per_branch:(cfg_index + 1) * per_branch]
         sp = UlyssesSelfAttention(layer, len(ranks), index, peer_exchange(group, ranks, index),
-                                  group_ranks=ranks, sparse=plan)
+                                  group_ranks=ranks, sparse=plan, head_chunks=args.head_chunks)
         x_local = x_branch[:, sp.partition(B.SEQ)].contiguous()
         del x_full
         stream = torch.cuda.current_stream(device)
         attn_events = []
 
         def step(record: bool):
-            s = sp.pre(x_local, rope, B.SEQ)
-            sp.exchange(*sp.send_recv_1(s))
-            if record:
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-            sp.attend(s)
-            if record:
-                e1.record(stream)
-                attn_events.append((e0, e1))
-            sp.exchange(*sp.send_recv_2(s))
-            return sp.post(s)
+            # The public layer call; the Ulysses object records events around
+            # each attention launch (one per head chunk) on the compute stream.
+            sp.attention_events = attn_events if record else None
+            try:
+                return sp(x_local, rope, B.SEQ)
+            finally:
+                sp.attention_events = None
 
         for _ in range(args.warmup):
             step(False)
@@ -76,7 +72,7 @@ def run_sequence_parallel(args) -> None:
             torch.cuda.synchronize()
         dist.barrier()
         ms = start.elapsed_time(stop) / args.steps
-        kernel_ms = sum(a.elapsed_time(b) for a, b in attn_events) / len(attn_events)
+        kernel_ms = sum(a.elapsed_time(b) for a, b in attn_events) / args.steps
         status = _native.read_status(device)
 
         # End to end through the public API with host buffers (pinned).
@@ -110,6 +106,9 @@ def run_sequence_parallel(args) -> None:
             achieved = local_attn_flop / (kernel_ms / 1e3) / 1e12
             layer_flop = B.LINEAR_FLOP + B.ATTN_FLOP * kept
             parallelism = f"cfg{cfg}xsp{world // cfg}" if cfg > 1 else f"sp{world}"
+            chunks = sp.chunks_for(B.SEQ)
+            if chunks > 1:
+                parallelism += f", {chunks} head chunks"
             if plan is not None:
                 workload = B.SPARSE_WORKLOAD + ", Ulysses SP (whole 128-token blocks per rank)"
                 kernel = "attn_fwd_bf16 (block-sparse instantiation)"
@@ -134,7 +133,7 @@ def run_sequence_parallel(args) -> None:
                         "ms_per_step": e2e_ms,
                         "h2d_bytes_per_step": host_x.numel() * host_x.element_size() * world,
                         "d2h_bytes_per_step": host_y.numel() * host_y.element_size() * world},
-                "gpu_launches": (4 if args.fp8 else 2) * args.steps,
+                "gpu_launches": (1 + (3 if args.fp8 else 1) * chunks) * args.steps,
                 "clocks": clock,
             }
             if plan is not None:

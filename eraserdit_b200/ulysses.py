@@ -29,6 +29,15 @@ floor-partitioned token range of the sequence (``mesh.py:163-169``) and all
 The two collectives are the only data-path communication; with CFG the
 Ulysses group is one branch's ranks (``eraserdit_b200.topology``).
 
+Head chunks (``head_chunks=C``, the reference's overlap pipeline
+``nccl_sequence.py:105-216``): each rank's Hl heads are split into C chunks of
+Hl / C.  The prologue writes the send buffer chunk-major
+(``send1[dest][chunk][token][qkv][b][head][d]``) so that every (destination,
+chunk) block is contiguous; then, on a communication stream, the exchange of
+chunk c + 1 runs while chunk c attends on the compute stream, and the finished
+chunk c returns while chunk c + 1 attends.  Every rank enqueues the exchanges
+in the same order (in 0, in 1, out 0, in 2, out 1, ...).
+
 With a block-sparse plan (``sparse=``) the sequence is in the plan's tile
 order, ranks own whole 128-token blocks (a floor partition of the blocks), and
 step 4 runs ``erd_attn_fwd_sparse_bf16`` with the plan's lists translated to
@@ -90,11 +99,12 @@ class _Step:
     length: int
     lengths: list
     start: int
-    send1: torch.Tensor
-    recv1: torch.Tensor
-    send2: torch.Tensor
-    recv2: torch.Tensor
+    send1: torch.Tensor  # [dest][chunk][token][qkv][b][hc][d]
+    recv1: torch.Tensor  # [chunk][src][slot token][qkv][b][hc][d]
+    send2: torch.Tensor  # [chunk][dest][FLAG | token][b][hc][d]
+    recv2: torch.Tensor  # [chunk][src][FLAG | token][b][hc][d]
     failed: bool = False
+    chunks: int = 1
 
 
 class UlyssesSelfAttention:
@@ -102,7 +112,7 @@ class UlyssesSelfAttention:
 
     def __init__(self, layer: EraserDiTSelfAttention, degree: int, rank: int,
                  exchange: Exchange, group_ranks: tuple[int, ...] | None = None,
-                 sparse=None) -> None:
+                 sparse=None, head_chunks: int | None = None) -> None:
         if layer.heads % degree:
             raise ValueError("attention heads must be divisible by Ulysses degree")
         if degree > 16:
@@ -119,6 +129,11 @@ class UlyssesSelfAttention:
             raise ValueError("the block-sparse path computes in BF16")
         self.sparse = sparse
         self._sparse_segments: dict[int, object] = {}
+        self.head_chunks = head_chunks  # None: select_head_chunks per call
+        self._comm_stream = None
+        # A list here collects (start, end) CUDA events around every attention
+        # launch on the stream it is enqueued on (for the benchmark's roofline).
+        self.attention_events: list | None = None
 
     def _bounds(self, length: int, rank: int) -> tuple[int, int]:
         if self.sparse is not None:
@@ -137,20 +152,31 @@ class UlyssesSelfAttention:
         start, end = self._bounds(length, self.rank)
         return slice(start, end)
 
-    def _buffers_for(self, batch: int, length: int, device, dtype):
-        key = (batch, length, device, dtype)
+    def chunks_for(self, length: int) -> int:
+        if self.head_chunks is not None:
+            chunks = self.head_chunks
+        else:
+            chunks = select_head_chunks(self.degree, length, self.local_heads,
+                                        sparse=self.sparse is not None)
+        if chunks < 1 or self.local_heads % chunks:
+            raise ValueError("head chunks must divide the heads per rank")
+        return chunks
+
+    def _buffers_for(self, batch: int, length: int, device, dtype, chunks: int = 1):
+        key = (batch, length, device, dtype, chunks)
         cached = self._buffers.get(key)
         if cached is None:
-            n, hl = self.degree, self.local_heads
+            n, hc = self.degree, self.local_heads // chunks
             lengths = self._lengths(length)
             lmax, lme = max(lengths), lengths[self.rank]
-            row1 = 3 * batch * hl * HEAD_DIM
-            row2 = batch * hl * HEAD_DIM
-            send1 = torch.empty(n, lme, 3, batch, hl, HEAD_DIM, device=device, dtype=dtype)
+            row1 = 3 * batch * hc * HEAD_DIM
+            row2 = batch * hc * HEAD_DIM
+            send1 = torch.empty(n, chunks, lme, 3, batch, hc, HEAD_DIM, device=device, dtype=dtype)
             # Zeroed once: slot rows past a shorter source's length stay finite.
-            recv1 = torch.zeros(n, lmax, 3, batch, hl, HEAD_DIM, device=device, dtype=dtype)
-            send2 = torch.zeros(n, FLAG + lmax * row2, device=device, dtype=dtype)
-            recv2 = torch.empty(n, FLAG + lme * row2, device=device, dtype=dtype)
+            recv1 = torch.zeros(chunks, n, lmax, 3, batch, hc, HEAD_DIM, device=device,
+                                dtype=dtype)
+            send2 = torch.zeros(chunks, n, FLAG + lmax * row2, device=device, dtype=dtype)
+            recv2 = torch.empty(chunks, n, FLAG + lme * row2, device=device, dtype=dtype)
             cached = (lengths, send1, recv1, send2, recv2, row1, row2)
             self._buffers[key] = cached
         return cached
@@ -159,8 +185,9 @@ class UlyssesSelfAttention:
     def pre(self, x_local: torch.Tensor, rope, length: int) -> _Step:
         """QKV projection + fused norm/RoPE straight into the send buffer."""
         batch = x_local.shape[0]
+        chunks = self.chunks_for(length)
         lengths, send1, recv1, send2, recv2, row1, _ = self._buffers_for(
-            batch, length, x_local.device, x_local.dtype)
+            batch, length, x_local.device, x_local.dtype, chunks)
         start, end = self._bounds(length, self.rank)
         if x_local.shape[1] != end - start:
             raise ValueError("local sequence length must match the rank's partition")
@@ -169,94 +196,148 @@ class UlyssesSelfAttention:
             rope = rope.in_order(self.sparse.order)
         qkv = self.layer.project_qkv(x_local)
         q, k, v = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN], qkv[..., 2 * HIDDEN:]
-        hl = self.local_heads
-        chunk = batch * hl * HEAD_DIM
+        hc = self.local_heads // chunks
+        chunk = batch * hc * HEAD_DIM
         base = send1.view(-1)
+        # (destination, head chunk) groups are contiguous blocks of L_rank tokens
         qk_norm_rope_into(
             q, k, self.layer.norm_q, self.layer.norm_k, self.layer.eps, rope,
             base[0:], base[chunk:], value=v, v_out=base[2 * chunk:], token_offset=start,
-            out_token_stride=row1, out_batch_stride=hl * HEAD_DIM, out_head_stride=HEAD_DIM,
-            heads_per_dest=hl, out_dest_stride=(end - start) * row1)
-        return _Step(batch, length, lengths, start, send1, recv1, send2, recv2)
+            out_token_stride=row1, out_batch_stride=hc * HEAD_DIM, out_head_stride=HEAD_DIM,
+            heads_per_dest=hc, out_dest_stride=(end - start) * row1)
+        return _Step(batch, length, lengths, start, send1, recv1, send2, recv2, chunks=chunks)
 
-    def send_recv_1(self, step: _Step) -> tuple[list, list]:
-        outputs = [step.recv1[s, :step.lengths[s]] for s in range(self.degree)]
-        inputs = [step.send1[d] for d in range(self.degree)]
+    def send_recv_1(self, step: _Step, chunk: int = 0) -> tuple[list, list]:
+        outputs = [step.recv1[chunk, s, :step.lengths[s]] for s in range(self.degree)]
+        inputs = [step.send1[d, chunk] for d in range(self.degree)]
         return outputs, inputs
 
-    def attend(self, step: _Step) -> None:
+    def attend(self, step: _Step, chunk: int = 0) -> None:
         """Attention over the received segments; rows go to their owners' chunks."""
+        events = self.attention_events
         try:
-            self._attend(step)
-            step.send2[:, :FLAG].zero_()
+            if events is not None:
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record()
+            self._attend(step, chunk)
+            if events is not None:
+                end.record()
+                events.append((start, end))
+            step.send2[chunk, :, :FLAG].zero_()
         except Exception:
             step.failed = True
-            step.send2[:, :FLAG].fill_(1.0)
+            step.send2[chunk, :, :FLAG].fill_(1.0)
             raise
         finally:
             self.calls += 1
 
-    def _attend(self, step: _Step) -> None:
+    def _attend(self, step: _Step, chunk: int = 0) -> None:
         from .attention import _segmented_call, fp8_workspace
-        n, hl, b = self.degree, self.local_heads, step.batch
+        n, b = self.degree, step.batch
+        hc = self.local_heads // step.chunks  # heads of this chunk
         lmax = max(step.lengths)
-        row1 = 3 * b * hl * HEAD_DIM
-        chunk = b * hl * HEAD_DIM
-        r = step.recv1.view(-1)
-        o = step.send2.view(-1)[FLAG:]
-        strides = (row1, HEAD_DIM, hl * HEAD_DIM, lmax * row1)  # token, head, batch, segment
-        o_strides = (b * hl * HEAD_DIM, HEAD_DIM, hl * HEAD_DIM, FLAG + lmax * b * hl * HEAD_DIM)
+        row1 = 3 * b * hc * HEAD_DIM  # one received token: q | k | v of every batch and head
+        qkv_gap = b * hc * HEAD_DIM   # from q to k (and k to v) inside a received token
+        r = step.recv1[chunk].view(-1)
+        o = step.send2[chunk].view(-1)[FLAG:]
+        strides = (row1, HEAD_DIM, hc * HEAD_DIM, lmax * row1)  # token, head, batch, segment
+        o_strides = (qkv_gap, HEAD_DIM, hc * HEAD_DIM, FLAG + lmax * qkv_gap)
+        q, k, v = r, r[qkv_gap:], r[2 * qkv_gap:]
         if self.sparse is not None:
             from .mask_sta import sparse_attention_into
             plan = self._sparse_segments.get(step.length)
             if plan is None:
                 plan = self.sparse.for_segments([l // 128 for l in step.lengths], lmax // 128)
                 self._sparse_segments[step.length] = plan
-            sparse_attention_into(r, r[chunk:], r[2 * chunk:], o, self.layer.softmax_scale, plan,
-                                  batch=b, heads=hl, seg_len=lmax, nseg=n, seg_lens=step.lengths,
-                                  q_strides=strides, k_strides=strides, v_strides=strides,
-                                  o_strides=o_strides)
+            sparse_attention_into(q, k, v, o, self.layer.softmax_scale, plan, batch=b, heads=hc,
+                                  seg_len=lmax, nseg=n, seg_lens=step.lengths, q_strides=strides,
+                                  k_strides=strides, v_strides=strides, o_strides=o_strides)
             return
         fp8 = self.layer.precision == "fp8"
-        extra = fp8_workspace(r.device, b, hl, lmax, n) if fp8 else ()
-        _segmented_call("erd_attn_fwd_fp8" if fp8 else "erd_attn_fwd_bf16", r, r[chunk:],
-                        r[2 * chunk:], o, self.layer.softmax_scale, batch=b, heads=hl,
-                        seg_len=lmax, nseg=n, seg_lens=step.lengths, q_strides=strides,
-                        k_strides=strides, v_strides=strides, o_strides=o_strides, extra=extra)
+        extra = fp8_workspace(r.device, b, hc, lmax, n) if fp8 else ()
+        _segmented_call("erd_attn_fwd_fp8" if fp8 else "erd_attn_fwd_bf16", q, k, v, o,
+                        self.layer.softmax_scale, batch=b, heads=hc, seg_len=lmax, nseg=n,
+                        seg_lens=step.lengths, q_strides=strides, k_strides=strides,
+                        v_strides=strides, o_strides=o_strides, extra=extra)
 
-    def send_recv_2(self, step: _Step) -> tuple[list, list]:
-        row2 = step.batch * self.local_heads * HEAD_DIM
-        outputs = [step.recv2[s] for s in range(self.degree)]
-        inputs = [step.send2[d, :FLAG + step.lengths[d] * row2] for d in range(self.degree)]
+    def send_recv_2(self, step: _Step, chunk: int = 0) -> tuple[list, list]:
+        row2 = step.batch * (self.local_heads // step.chunks) * HEAD_DIM
+        outputs = [step.recv2[chunk, s] for s in range(self.degree)]
+        inputs = [step.send2[chunk, d, :FLAG + step.lengths[d] * row2]
+                  for d in range(self.degree)]
         return outputs, inputs
 
     def post(self, step: _Step) -> torch.Tensor:
         """Peer error check, head gather, output projection."""
-        flags = step.recv2[:, 0].float()
+        flags = step.recv2[:, :, 0].float().amax(dim=0)
         if step.failed:
             raise RuntimeError("local sequence-parallel attention failed")
         bad = torch.nonzero(flags != 0).flatten().tolist()
         if bad:
             raise SequenceParallelPeerError(tuple(self.group_ranks[i] for i in bad))
         lme = step.lengths[self.rank]
-        n, hl, b = self.degree, self.local_heads, step.batch
-        heads = step.recv2[:, FLAG:].view(n, lme, b, hl, HEAD_DIM)
-        attn = heads.permute(2, 1, 0, 3, 4).reshape(b, lme, n * hl * HEAD_DIM)
+        n, c, b = self.degree, step.chunks, step.batch
+        hc = self.local_heads // c
+        # head = source rank * Hl + chunk * Hc + head within the chunk
+        heads = step.recv2[:, :, FLAG:].view(c, n, lme, b, hc, HEAD_DIM)
+        attn = heads.permute(3, 2, 1, 0, 4, 5).reshape(b, lme, n * c * hc * HEAD_DIM)
         return self.layer.project_out(attn)
 
     # -------------------------------------------------------------- forward
     def forward(self, x_local: torch.Tensor, rope, length: int) -> torch.Tensor:
         """Layer output for this rank's tokens [B, L_rank, 2048]."""
         step = self.pre(x_local, rope, length)
-        out1, in1 = self.send_recv_1(step)
-        self.exchange(out1, in1)
+        if step.chunks > 1 and x_local.is_cuda:
+            return self._forward_pipelined(step)
+        error = None
+        for c in range(step.chunks):
+            out1, in1 = self.send_recv_1(step, c)
+            self.exchange(out1, in1)
+            try:
+                self.attend(step, c)
+            except Exception as exc:  # every rank still enters the second exchange
+                error = error or exc
+            out2, in2 = self.send_recv_2(step, c)
+            self.exchange(out2, in2)
+        if error is not None:
+            raise error
+        return self.post(step)
+
+    def _forward_pipelined(self, step: _Step) -> torch.Tensor:
+        """Exchanges on a communication stream, attention on the current one:
+        in(c + 1) and out(c) overlap attend(c + 1) / attend(c)."""
+        device = step.send1.device
+        current = torch.cuda.current_stream(device)
+        if self._comm_stream is None:
+            self._comm_stream = torch.cuda.Stream(device=device)
+        comm = self._comm_stream
+        comm.wait_stream(current)  # send buffers written by the prologue
+
+        def exchange_in(c):
+            with torch.cuda.stream(comm):
+                self.exchange(*self.send_recv_1(step, c))
+                ready = torch.cuda.Event()
+                ready.record(comm)
+            return ready
+
         error = None
         try:
-            self.attend(step)
-        except Exception as exc:  # every rank still enters the second exchange
-            error = exc
-        out2, in2 = self.send_recv_2(step)
-        self.exchange(out2, in2)
+            ready = exchange_in(0)
+            for c in range(step.chunks):
+                current.wait_event(ready)
+                try:
+                    self.attend(step, c)
+                except Exception as exc:  # every rank still enters every exchange
+                    error = error or exc
+                done = torch.cuda.Event()
+                done.record(current)
+                if c + 1 < step.chunks:
+                    ready = exchange_in(c + 1)
+                with torch.cuda.stream(comm):
+                    comm.wait_event(done)
+                    self.exchange(*self.send_recv_2(step, c))
+        finally:
+            current.wait_stream(comm)
         if error is not None:
             raise error
         return self.post(step)
@@ -264,15 +345,31 @@ class UlyssesSelfAttention:
     __call__ = forward
 
 
+def select_head_chunks(degree: int, length: int, local_heads: int, *, sparse: bool = False) -> int:
+    """Head chunks of the overlap pipeline for one Ulysses layer call.
+
+    Mirrors ``layers/attention/ulysses_policy.py:5-17``: a measured policy that
+    depends only on shapes, so that every rank takes the same collective steps.
+    Measured on 8 B200s at 2 x 32640 tokens (ms per layer, 1 / 2 / 4 chunks):
+    SP2 14.14 / 14.04 / 14.42, SP4 7.34 / 7.26 / 7.84, SP8 3.94 / 4.23 / 4.20,
+    SP8 sparse 1.92 / 1.91, SP4 FP8 8.59 / 8.68.  The exchanges are 5-8 % of a
+    layer over NVLink, so overlapping them gains at most 1 %, and smaller
+    attention launches (fewer heads per chunk) lose more than that at SP8: one
+    exchange per direction everywhere.
+    """
+    del degree, length, local_heads, sparse
+    return 1
+
+
 def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, rope,
-                  sparse=None) -> list[torch.Tensor]:
+                  sparse=None, head_chunks: int | None = None) -> list[torch.Tensor]:
     """Run all ``degree`` ranks of the Ulysses layer inside one process on one
     device, exchanging chunks by copies (the same buffers and kernels as the
     NCCL path).  Returns each rank's output; used to check the data layout on
     a single GPU."""
     length = x.shape[1]
-    ranks = [UlyssesSelfAttention(layer, degree, r, exchange=None, sparse=sparse)
-             for r in range(degree)]
+    ranks = [UlyssesSelfAttention(layer, degree, r, exchange=None, sparse=sparse,
+                                  head_chunks=head_chunks) for r in range(degree)]
     steps = []
     for r in ranks:
         sl = r.partition(length)
@@ -284,8 +381,9 @@ def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, r
             for src in range(degree):
                 outputs[src].copy_(pairs[src][1][dst])
 
-    all_to_all([r.send_recv_1(s) for r, s in zip(ranks, steps)])
-    for r, s in zip(ranks, steps):
-        r.attend(s)
-    all_to_all([r.send_recv_2(s) for r, s in zip(ranks, steps)])
+    for c in range(steps[0].chunks):
+        all_to_all([r.send_recv_1(s, c) for r, s in zip(ranks, steps)])
+        for r, s in zip(ranks, steps):
+            r.attend(s, c)
+        all_to_all([r.send_recv_2(s, c) for r, s in zip(ranks, steps)])
     return [r.post(s) for r, s in zip(ranks, steps)]

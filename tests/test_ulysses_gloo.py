@@ -1,6 +1,7 @@
 """Ulysses exchange protocol on 2 CPU ranks (gloo): chunk routing, uneven shards,
-and peer-failure propagation with both collectives always entered (the
-reference's tests/test_ulysses_overlap.py:47-60 injects a failing impl the same way).
+head chunks, and peer-failure propagation with every collective always entered
+(the reference's tests/test_ulysses_overlap.py:47-60 injects a failing impl the
+same way).
 
 The CUDA phases are replaced by CPU stand-ins that move the same buffers, so
 only the host protocol is under test here; the GPU tests cover the kernels."""
@@ -34,53 +35,60 @@ def _rank(rank, world, port, result_dir):
             heads, softmax_scale, eps = 4, 0.125, 1e-6
 
         class CpuUlysses(UlyssesSelfAttention):
-            """Stand-in phases: send chunk d carries (rank, d, token) tags."""
+            """Stand-in phases: send block (d, chunk c) carries (c, rank, d, token) tags."""
             broken = False
 
             def pre(self, x_local, rope, length):
                 lengths = floor_lengths(length, self.degree)
                 lme = lengths[self.rank]
-                n, b = self.degree, x_local.shape[0]
-                send1 = torch.empty(n, lme, 1)
+                n, b, chunks = self.degree, x_local.shape[0], self.head_chunks
+                send1 = torch.empty(n, chunks, lme, 1)
                 for d in range(n):
-                    send1[d, :, 0] = 1000 * self.rank + 100 * d + torch.arange(lme)
-                recv1 = torch.zeros(n, max(lengths), 1)
-                send2 = torch.zeros(n, FLAG + max(lengths))
-                recv2 = torch.empty(n, FLAG + lme)
+                    for c in range(chunks):
+                        send1[d, c, :, 0] = (10000 * c + 1000 * self.rank + 100 * d
+                                             + torch.arange(lme))
+                recv1 = torch.zeros(chunks, n, max(lengths), 1)
+                send2 = torch.zeros(chunks, n, FLAG + max(lengths))
+                recv2 = torch.empty(chunks, n, FLAG + lme)
                 from eraserdit_b200.ulysses import _Step
-                return _Step(b, length, lengths, 0, send1, recv1, send2, recv2)
+                return _Step(b, length, lengths, 0, send1, recv1, send2, recv2, chunks=chunks)
 
-            def send_recv_2(self, step):
-                outputs = [step.recv2[s] for s in range(self.degree)]
-                inputs = [step.send2[d, :FLAG + step.lengths[d]] for d in range(self.degree)]
+            def send_recv_2(self, step, chunk=0):
+                outputs = [step.recv2[chunk, s] for s in range(self.degree)]
+                inputs = [step.send2[chunk, d, :FLAG + step.lengths[d]]
+                          for d in range(self.degree)]
                 return outputs, inputs
 
-            def _attend(self, step):
-                if self.broken:
+            def _attend(self, step, chunk=0):
+                if self.broken and chunk == step.chunks - 1:
                     raise RuntimeError("injected attention failure")
                 for s in range(self.degree):
-                    got = step.recv1[s, :step.lengths[s], 0]
-                    expect = 1000 * s + 100 * self.rank + torch.arange(step.lengths[s])
+                    got = step.recv1[chunk, s, :step.lengths[s], 0]
+                    expect = (10000 * chunk + 1000 * s + 100 * self.rank
+                              + torch.arange(step.lengths[s]))
                     assert torch.equal(got, expect.float())
-                    step.send2[s, FLAG:FLAG + step.lengths[s]] = got + 0.5
+                    step.send2[chunk, s, FLAG:FLAG + step.lengths[s]] = got + 0.5
 
             def post(self, step):
-                flags = step.recv2[:, 0]
+                flags = step.recv2[:, :, 0].amax(dim=0)
                 if step.failed:
                     raise RuntimeError("local sequence-parallel attention failed")
                 bad = torch.nonzero(flags != 0).flatten().tolist()
                 if bad:
                     raise SequenceParallelPeerError(tuple(bad))
-                return step.recv2[:, FLAG:].clone()
+                return step.recv2[:, :, FLAG:].clone()
 
-        sp = CpuUlysses(Layer(), world, rank, peer_exchange(None, tuple(range(world)), rank))
         outcomes = []
-        for length in (8, 7, 11):
-            out = sp(torch.zeros(2, floor_lengths(length, world)[rank], 1), None, length)
-            lme = floor_lengths(length, world)[rank]
-            for s in range(world):
-                expect = 1000 * rank + 100 * s + torch.arange(lme) + 0.5
-                assert torch.equal(out[s], expect.float())
+        for chunks in (1, 2):
+            sp = CpuUlysses(Layer(), world, rank, peer_exchange(None, tuple(range(world)), rank),
+                            head_chunks=chunks)
+            for length in (8, 7, 11):
+                out = sp(torch.zeros(2, floor_lengths(length, world)[rank], 1), None, length)
+                lme = floor_lengths(length, world)[rank]
+                for c in range(chunks):
+                    for s in range(world):
+                        expect = 10000 * c + 1000 * rank + 100 * s + torch.arange(lme) + 0.5
+                        assert torch.equal(out[c, s], expect.float())
             outcomes.append("ok")
         sp.broken = rank == 1
         try:
@@ -105,5 +113,5 @@ def test_two_rank_exchange_and_peer_failure():
                            start_method="spawn")
         r0 = open(os.path.join(d, "r0")).read().split("|")
         r1 = open(os.path.join(d, "r1")).read().split("|")
-    assert r0 == ["ok", "ok", "ok", "peer (1,)", "ok"]
-    assert r1 == ["ok", "ok", "ok", "injected attention failure", "ok"]
+    assert r0 == ["ok", "ok", "peer (1,)", "ok"]
+    assert r1 == ["ok", "ok", "injected attention failure", "ok"]

@@ -43,3 +43,16 @@ def test_sp8_full_size_matches_single_gpu():
     got = torch.cat(emulate_ranks(layer, 8, x, rope), dim=1)
     assert max_abs(got, want) <= 1e-2  # one BF16 ulp at |y| ~ 1: KV blocks split per segment
     assert cosine(got, want) >= 0.99999
+
+
+@pytest.mark.parametrize("degree,chunks", [(2, 2), (2, 4), (4, 2), (8, 4)])
+def test_head_chunks_bitwise_equal_unchunked(degree, chunks):
+    """The head-chunk layout changes only the exchange granularity: every
+    rank's output equals the unchunked one bit for bit (as the reference's
+    tests/test_ulysses_overlap.py:38-45 requires)."""
+    from eraserdit_b200.ulysses import emulate_ranks
+    layer, rope, x = _setup(2, 8, 12, 2, seed=degree)
+    plain = emulate_ranks(layer, degree, x, rope, head_chunks=1)
+    chunked = emulate_ranks(layer, degree, x, rope, head_chunks=chunks)
+    for a, b in zip(plain, chunked):
+        assert torch.equal(a, b)

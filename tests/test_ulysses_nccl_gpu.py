@@ -47,6 +47,11 @@ def _rank(rank, world, port, out_dir):
             cos = float(torch.nn.functional.cosine_similarity(
                 got.float().flatten(), want[:, sl].float().flatten(), dim=0))
             assert err <= 1e-2 and cos >= 0.99999, (err, cos)
+            # head chunks: exchanges on a second stream overlap the chunks' attention
+            chunked = UlyssesSelfAttention(layer, world, index, peer_exchange(group, ranks, index),
+                                           ranks, head_chunks=2)
+            again = chunked(x[:, sl].contiguous(), rope, x.shape[1])
+            assert torch.equal(again, got), "head chunks changed the result"
         # block-sparse attention over the exchange (whole 128-token blocks per rank)
         from eraserdit_b200 import sparse_pattern as sp_pattern
         from eraserdit_b200.mask_sta import SparsePlan
