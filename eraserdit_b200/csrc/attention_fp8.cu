@@ -8,9 +8,11 @@
 //   softmax(Q K^T) unchanged;  Q and the smoothed K are quantised to E4M3 with
 //   one scale per 128-token block (amax / 448);  V is quantised to E4M3 with one
 //   scale per (batch, head, channel) over all tokens (amax / 448, as
-//   sage_peripheral.py:76-77);  P = 2^(S - max) <= 1 is quantised to E4M3 after
-//   scaling by 448;  both products accumulate in FP32 (tcgen05 kind::f8f6f4,
-//   accumulators in TMEM); the V scales and 1/448 are applied in the epilogue.
+//   sage_peripheral.py:76-77);  P = 2^(S - m) is quantised to E4M3 after
+//   scaling by 448 / 4, with m a running row max that may lag the true one by
+//   up to 2 (log2 units) before O is rescaled, so P * 112 <= 448 always fits;
+//   both products accumulate in FP32 (tcgen05 kind::f8f6f4, accumulators in
+//   TMEM); the V scales and the P scale are applied in the epilogue.
 //
 // Three kernels run on the caller's stream over a caller-provided workspace:
 //   fp8_stats     per-chunk partial K sums and V abs-maxima per channel;
@@ -41,6 +43,8 @@ constexpr int kChunks = 16;                   // token chunks of the statistics 
 constexpr float kE4M3Max = 448.0f;
 constexpr int kMaxSegments = 16;
 constexpr float kLog2E4M3Max = 8.807354922057604f;  // log2(448)
+constexpr float kStale = 2.0f;
+constexpr float kStaleScale = 4.0f;  // 2^kStale
 // Of every 8 column pairs, this many take the FMA-pipe exp2 (as in the BF16
 // kernel), the rest MUFU ex2.
 #ifndef ERD_FP8_POLY_EVERY8
@@ -457,13 +461,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l_run = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
+      const float skj = __ldg(sk + j);  // read before the wait: its latency hides there
       if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->s_full[t]), j & 1, abort, p.status,
                                              kStatusTimeoutSoftmax))) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const float c = cq * __ldg(sk + j);
+      const float c = cq * skj;
       int seg, l0;
       tile_coords(j, p.g.tiles_per_seg, seg, l0);
       const int valid = min(kBlock, p.g.seg_lens[seg] - l0);
@@ -471,17 +476,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       {
         uint32_t sr[128];
         tmem_ld_wait_128(tS, sr);
+        if (valid < kBlock) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i >= valid) sr[i] = __float_as_uint(-CUDART_INF_F);
+        }
 #pragma unroll
         for (int i = 0; i < 128; i += 4) {
-          mx0 = fmax3(mx0, i < valid ? __uint_as_float(sr[i]) : -CUDART_INF_F,
-                      i + 1 < valid ? __uint_as_float(sr[i + 1]) : -CUDART_INF_F);
-          mx1 = fmax3(mx1, i + 2 < valid ? __uint_as_float(sr[i + 2]) : -CUDART_INF_F,
-                      i + 3 < valid ? __uint_as_float(sr[i + 3]) : -CUDART_INF_F);
+          mx0 = fmax3(mx0, __uint_as_float(sr[i]), __uint_as_float(sr[i + 1]));
+          mx1 = fmax3(mx1, __uint_as_float(sr[i + 2]), __uint_as_float(sr[i + 3]));
         }
       }
       const float m_tile = fmaxf(mx0, mx1) * c;
-      const bool rescale = m_tile > m_run && j > 0;
-      const float m_new = fmaxf(m_run, m_tile);
+      // The running max may lag the true one by up to kStale (log2 units): P is
+      // scaled by 448 * 2^-kStale so that it still fits E4M3.
+      const bool grow = m_tile > m_run + kStale;
+      const bool rescale = grow && j > 0;
+      const float m_new = grow ? m_tile : m_run;
       if (j > 0) {
         if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->o_done[t]), (j - 1) & 1, abort,
                                                p.status, kStatusTimeoutSoftmax))) {
@@ -505,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       m_run = m_new;
       // P * 448 = 2^(S c - m + log2 448): the E4M3 range scaling rides in the
       // exponent; the row sum is of P * 448 and divided by 448 at the end.
-      const float bias = kLog2E4M3Max - m_new;
+      const float bias = kLog2E4M3Max - kStale - m_new;
       float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -539,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_st16(tP + h * 16, pk);
       }
-      l_run += (sum0 + sum1) * (1.0f / kE4M3Max);
+      l_run += (sum0 + sum1) * (kStaleScale / kE4M3Max);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(smem_u32(&bars->p_full[t]));
@@ -555,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile_coords(qt, p.g.tiles_per_seg, seg, l0);
         const int tok = l0 + row;
         if (tok < p.g.seg_lens[seg]) {
-          const float inv = 1.0f / (l_run * kE4M3Max);
+          const float inv = kStaleScale / (l_run * kE4M3Max);
           const float* sv = p.sv + static_cast<size_t>(bh) * kDim;
           __nv_bfloat16* dst =
               p.out + seg * p.lo.ss + batch * p.lo.bs + head * p.lo.hs + tok * p.lo.ts;
