@@ -112,18 +112,19 @@ def read_status(device: torch.device, reset: bool = True) -> int:
     return value
 
 
-_workspaces: dict[int, torch.Tensor] = {}
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
 
 def workspace(device: torch.device, nbytes: int) -> int:
     """Address of a caller-owned, 1024-byte aligned device buffer of at least
-    ``nbytes`` (grown on demand, reused across calls on this device's stream
-    order)."""
+    ``nbytes`` for work enqueued on the current stream of ``device`` (one buffer
+    per stream, grown on demand, reused in that stream's order)."""
     index = device.index if device.index is not None else torch.cuda.current_device()
-    buf = _workspaces.get(index)
+    key = (index, stream_handle(torch.device("cuda", index)))
+    buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes + 1024:
         buf = torch.empty(nbytes + 1024, dtype=torch.uint8, device=torch.device("cuda", index))
-        _workspaces[index] = buf
+        _workspaces[key] = buf
     base = buf.data_ptr()
     return (base + 1023) // 1024 * 1024
 

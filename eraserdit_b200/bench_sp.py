@@ -15,6 +15,13 @@ import torch
 import torch.distributed as dist
 
 
+def _alternate(objects, counter, xd, rope, length):
+    """Call the Ulysses objects in turn (step i uses objects[i % 2])."""
+    sp = objects[counter[0] % len(objects)]
+    counter[0] += 1
+    return sp(xd, rope, length)
+
+
 def run_sequence_parallel(args) -> None:
     import bench as B
     from eraserdit_b200 import _native
@@ -75,20 +82,18 @@ def run_sequence_parallel(args) -> None:
         kernel_ms = sum(a.elapsed_time(b) for a, b in attn_events) / args.steps
         status = _native.read_status(device)
 
-        # End to end through the public API with host buffers (pinned).
+        # End to end through the public API with host buffers (pinned).  Steps
+        # alternate between two streams, each with its own Ulysses object (their
+        # exchange buffers are per object); every rank issues the exchanges of
+        # both in the same order.
         host_x = x_local.cpu().pin_memory()
-        host_y = torch.empty_like(host_x).pin_memory()
-        for _ in range(max(args.warmup, 1)):
-            host_y.copy_(sp(host_x.to(device, non_blocking=True), rope, B.SEQ), non_blocking=True)
-        torch.cuda.synchronize()
+        host_y = [torch.empty_like(host_x).pin_memory() for _ in range(2)]
+        sp2 = UlyssesSelfAttention(layer, len(ranks), index, peer_exchange(group, ranks, index),
+                                   group_ranks=ranks, sparse=plan, head_chunks=args.head_chunks)
+        objects = [sp, sp2]
         dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            host_y.copy_(sp(host_x.to(device, non_blocking=True), rope, B.SEQ), non_blocking=True)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        e2e_ms = e0.elapsed_time(e1) / args.steps
+        e2e_ms = B.run_e2e(lambda xd, i=[0]: _alternate(objects, i, xd, rope, B.SEQ), host_x,
+                           host_y, device, args.warmup, args.steps)
 
         stats = torch.tensor([ms, kernel_ms, e2e_ms, float(status)], device=device)
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
@@ -132,7 +137,8 @@ def run_sequence_parallel(args) -> None:
                 "e2e": {"value": layer_flop / (e2e_ms / 1e3) / 1e12, "unit": B.UNIT,
                         "ms_per_step": e2e_ms,
                         "h2d_bytes_per_step": host_x.numel() * host_x.element_size() * world,
-                        "d2h_bytes_per_step": host_y.numel() * host_y.element_size() * world},
+                        "d2h_bytes_per_step": host_y[0].numel() * host_y[0].element_size() * world,
+                        "streams": 2},
                 "gpu_launches": (1 + (3 if args.fp8 else 1) * chunks) * args.steps,
                 "clocks": clock,
             }
