@@ -435,6 +435,8 @@ def main() -> None:
                         help="Sage-style FP8 attention (configuration 3) instead of BF16")
     parser.add_argument("--sparse", action="store_true",
                         help="mask-aware block-sparse attention (configuration 4)")
+    parser.add_argument("--transport", default="peer", choices=["peer", "nccl"],
+                        help="Ulysses exchange: peer-memory stores over NVLink or NCCL all-to-all")
     parser.add_argument("--head-chunks", type=int, default=None,
                         help="Ulysses head chunks (exchange/attention overlap); default: policy")
     args = parser.parse_args()

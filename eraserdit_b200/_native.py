@@ -19,7 +19,7 @@ from pathlib import Path
 import torch
 
 LIBRARY_PATH = Path(__file__).resolve().parent / "liberaserdit_b200.so"
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _c_int, _c_i64, _c_float, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -41,6 +41,19 @@ SIGNATURES = {
                                 + [_vp, _c_int, _vp, _c_i64, _vp, _vp, _vp],
     "erd_gather_tokens": [_vp, _c_i64, _c_i64, _c_int, _vp, _c_i64, _c_i64, _vp, _c_int, _c_int,
                           _c_int, _vp],
+    "erd_qk_norm_rope_peer": [_vp, _vp, _vp, _c_i64, _c_i64, _c_int, _c_int, _c_int, _vp, _vp,
+                              _c_float, _c_int, _vp, _vp, _c_i64, _c_i64, _vp, _c_int, _c_int,
+                              _c_int, _c_int, _c_int, _vp, _vp, _c_int, _c_i64, _c_i64, _c_i64,
+                              _c_i64, _c_i64, _c_int, _vp],
+    "erd_attn_fwd_bf16_peer": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 4
+                              + [_vp, _c_int, _c_float, _vp] + [_c_i64] * 3 + [_vp, _vp],
+    "erd_peer_alloc": [ctypes.c_size_t, ctypes.POINTER(_vp)],
+    "erd_peer_free": [_vp],
+    "erd_peer_ipc_handle": [_vp, _vp],
+    "erd_peer_ipc_open": [_vp, ctypes.POINTER(_vp)],
+    "erd_peer_ipc_close": [_vp],
+    "erd_peer_signal": [_vp, _c_int, ctypes.c_int32, _vp],
+    "erd_peer_wait": [_vp, _c_int, ctypes.c_int32, _c_i64, _vp, _vp],
     "erd_attn_fp8_workspace_bytes": [_c_int, _c_int, _c_int, _c_int],
     "erd_attn_fwd_fp8": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 4 + [_vp, _c_int, _c_float,
                                                                            _vp] + [_c_i64] * 4

@@ -50,8 +50,11 @@ def run_sequence_parallel(args) -> None:
         x_full = torch.randn(B.BATCH, B.SEQ, B.HIDDEN, generator=g, device=device).bfloat16()
         per_branch = B.BATCH // cfg
         x_branch = x_full[cfg_index * per_branch:(cfg_index + 1) * per_branch]
+        # The peer transport serves the dense BF16 path; FP8 and sparse use NCCL.
+        transport = args.transport if not (args.fp8 or args.sparse) else "nccl"
         sp = UlyssesSelfAttention(layer, len(ranks), index, peer_exchange(group, ranks, index),
-                                  group_ranks=ranks, sparse=plan, head_chunks=args.head_chunks)
+                                  group_ranks=ranks, sparse=plan, head_chunks=args.head_chunks,
+                                  transport=transport, group=group)
         x_local = x_branch[:, sp.partition(B.SEQ)].contiguous()
         del x_full
         stream = torch.cuda.current_stream(device)
@@ -89,7 +92,8 @@ def run_sequence_parallel(args) -> None:
         host_x = x_local.cpu().pin_memory()
         host_y = [torch.empty_like(host_x).pin_memory() for _ in range(2)]
         sp2 = UlyssesSelfAttention(layer, len(ranks), index, peer_exchange(group, ranks, index),
-                                   group_ranks=ranks, sparse=plan, head_chunks=args.head_chunks)
+                                   group_ranks=ranks, sparse=plan, head_chunks=args.head_chunks,
+                                   transport=transport, group=group)
         objects = [sp, sp2]
         dist.barrier()
         e2e_ms = B.run_e2e(lambda xd, i=[0]: _alternate(objects, i, xd, rope, B.SEQ), host_x,
@@ -98,6 +102,11 @@ def run_sequence_parallel(args) -> None:
         stats = torch.tensor([ms, kernel_ms, e2e_ms, float(status)], device=device)
         dist.all_reduce(stats, op=dist.ReduceOp.MAX)
         ms, kernel_ms, e2e_ms, status = stats.tolist()
+        # every rank's exchanges are done: release the peer buffers
+        torch.cuda.synchronize()
+        dist.barrier()
+        sp.close()
+        sp2.close()
         clock = clocks.summary()
         if rank == 0:
             if status:
@@ -111,6 +120,7 @@ def run_sequence_parallel(args) -> None:
             achieved = local_attn_flop / (kernel_ms / 1e3) / 1e12
             layer_flop = B.LINEAR_FLOP + B.ATTN_FLOP * kept
             parallelism = f"cfg{cfg}xsp{world // cfg}" if cfg > 1 else f"sp{world}"
+            parallelism += f", {transport} exchange"
             chunks = sp.chunks_for(B.SEQ)
             if chunks > 1:
                 parallelism += f", {chunks} head chunks"

@@ -77,6 +77,9 @@ struct AttnParams {
   const uint32_t* entries;   // key tile | A halves << 24 | B halves << 26
   long long n_entries;
   const int* out_rows;       // optional (one segment): output token of each query row
+  // Optional per-segment output bases (another rank's return buffer); when set
+  // they replace out + segment * o_ss.
+  __nv_bfloat16* seg_out[kMaxSegments];
 };
 
 constexpr uint32_t kEntryTileMask = (1u << 24) - 1;
@@ -434,8 +437,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tok < p.seg_lens[seg]) {
           const float inv_l = 1.0f / l_run;
           const long long out_tok = (kSparse && p.out_rows != nullptr) ? __ldg(p.out_rows + tok) : tok;
-          __nv_bfloat16* dst =
-              p.out + seg * p.o_ss + batch * p.o_bs + head * p.o_hs + out_tok * p.o_rs;
+          __nv_bfloat16* seg_base = p.seg_out[seg] != nullptr ? p.seg_out[seg] : p.out + seg * p.o_ss;
+          __nv_bfloat16* dst = seg_base + batch * p.o_bs + head * p.o_hs + out_tok * p.o_rs;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
 #pragma unroll
@@ -555,6 +558,7 @@ int prepare(const void* q, const void* k, const void* v, int64_t q_token_stride,
   p.entries = nullptr;
   p.n_entries = 0;
   p.out_rows = nullptr;
+  for (int s = 0; s < kMaxSegments; ++s) p.seg_out[s] = nullptr;
   return kErrOk;
 }
 
@@ -622,4 +626,29 @@ extern "C" int erd_attn_fwd_sparse_bf16(
   L.p.n_entries = n_entries;
   L.p.out_rows = out_rows;
   return launch<true>(L, static_cast<unsigned>(n_schedule), heads, batch, stream);
+}
+
+extern "C" int erd_attn_fwd_bf16_peer(
+    const void* q, const void* k, const void* v, int64_t q_token_stride, int64_t q_head_stride,
+    int64_t q_batch_stride, int64_t q_seg_stride, int64_t k_token_stride, int64_t k_head_stride,
+    int64_t k_batch_stride, int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+    int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads, int seg_len, int nseg,
+    const int32_t* seg_lens, int head_dim, float softmax_scale, void* const* seg_out,
+    int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride, int* status,
+    void* stream) {
+  if (seg_out == nullptr) return kErrNullPointer;
+  if (nseg <= 0 || nseg > kMaxSegments) return kErrBadShape;
+  for (int s = 0; s < nseg; ++s) {
+    if (seg_out[s] == nullptr) return kErrNullPointer;
+    if (!aligned16(seg_out[s])) return kErrMisaligned;
+  }
+  Launch L;
+  if (int rc = prepare(q, k, v, q_token_stride, q_head_stride, q_batch_stride, q_seg_stride,
+                       k_token_stride, k_head_stride, k_batch_stride, k_seg_stride,
+                       v_token_stride, v_head_stride, v_batch_stride, v_seg_stride, batch, heads,
+                       seg_len, nseg, seg_lens, head_dim, softmax_scale, seg_out[0],
+                       o_token_stride, o_head_stride, o_batch_stride, 0, status, &L))
+    return rc;
+  for (int s = 0; s < nseg; ++s) L.p.seg_out[s] = static_cast<__nv_bfloat16*>(seg_out[s]);
+  return launch<false>(L, static_cast<unsigned>((L.p.q_tiles + 1) / 2), heads, batch, stream);
 }

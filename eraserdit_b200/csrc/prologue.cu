@@ -44,6 +44,11 @@ struct PrologueParams {
   __nv_bfloat16* v_out;
   long long out_ts, out_bs, out_hs, out_ds;
   int heads_per_dest;
+  // Peer mode: head group g goes to dest_base[g] (another rank's receive
+  // buffer), Q at +0, K at +k_rel, V at +v_rel elements.
+  __nv_bfloat16* dest_base[16];
+  long long k_rel, v_rel;
+  int peer;
 };
 
 __device__ __forceinline__ float bf16_round(float x) {
@@ -117,8 +122,9 @@ __global__ void __launch_bounds__(kTokensPerBlock * 32, 3)
       const int head = c0 / kHeadDimP;
       const int dest = head / p.heads_per_dest;
       const int hl = head - dest * p.heads_per_dest;
-      *reinterpret_cast<uint4*>(p.v_out + b * p.out_bs + t * p.out_ts + hl * p.out_hs +
-                                dest * p.out_ds + (c0 - head * kHeadDimP)) = vv[it];
+      const long long off = b * p.out_bs + t * p.out_ts + hl * p.out_hs + (c0 - head * kHeadDimP);
+      __nv_bfloat16* dst = p.peer ? p.dest_base[dest] + p.v_rel : p.v_out + dest * p.out_ds;
+      *reinterpret_cast<uint4*>(dst + off) = vv[it];
     }
   }
 
@@ -226,9 +232,15 @@ __global__ void __launch_bounds__(kTokensPerBlock * 32, 3)
     const int d0 = c0 - head * kHeadDimP;
     const int dest = head / p.heads_per_dest;
     const int hl = head - dest * p.heads_per_dest;
-    const long long off = b * p.out_bs + t * p.out_ts + hl * p.out_hs + dest * p.out_ds + d0;
-    *reinterpret_cast<uint4*>(p.q_out + off) = pack8(q);
-    *reinterpret_cast<uint4*>(p.k_out + off) = pack8(k);
+    const long long off = b * p.out_bs + t * p.out_ts + hl * p.out_hs + d0;
+    if (p.peer) {
+      __nv_bfloat16* base = p.dest_base[dest];
+      *reinterpret_cast<uint4*>(base + off) = pack8(q);
+      *reinterpret_cast<uint4*>(base + p.k_rel + off) = pack8(k);
+    } else {
+      *reinterpret_cast<uint4*>(p.q_out + dest * p.out_ds + off) = pack8(q);
+      *reinterpret_cast<uint4*>(p.k_out + dest * p.out_ds + off) = pack8(k);
+    }
   }
 }
 
@@ -278,17 +290,24 @@ extern "C" int erd_rope_axis_table(const float* freqs, int nfreq, int frames, in
   return static_cast<int>(cudaGetLastError());
 }
 
-extern "C" int erd_qk_norm_rope(const void* q_in, const void* k_in, const void* v_in,
-                                int64_t in_token_stride, int64_t in_batch_stride, int batch,
-                                int tokens, int hidden, const void* q_weight, const void* k_weight,
-                                float eps, int rope_mode, const float* cos_tab,
-                                const float* sin_tab, int64_t tab_token_stride,
-                                int64_t tab_batch_stride, const float* axis_table, int nfreq,
-                                int frames, int height, int width, int token_offset,
-                                const int32_t* grid_index, void* q_out,
-                                void* k_out, void* v_out, int64_t out_token_stride,
-                                int64_t out_batch_stride, int64_t out_head_stride,
-                                int heads_per_dest, int64_t out_dest_stride, void* stream) {
+namespace {
+
+struct PeerOut {
+  void* const* dest_bases;
+  int ndest;
+  int64_t k_rel, v_rel;
+};
+
+int qk_norm_rope_impl(const void* q_in, const void* k_in, const void* v_in,
+                      int64_t in_token_stride, int64_t in_batch_stride, int batch, int tokens,
+                      int hidden, const void* q_weight, const void* k_weight, float eps,
+                      int rope_mode, const float* cos_tab, const float* sin_tab,
+                      int64_t tab_token_stride, int64_t tab_batch_stride,
+                      const float* axis_table, int nfreq, int frames, int height, int width,
+                      int token_offset, const int32_t* grid_index, void* q_out, void* k_out,
+                      void* v_out, int64_t out_token_stride, int64_t out_batch_stride,
+                      int64_t out_head_stride, int heads_per_dest, int64_t out_dest_stride,
+                      const PeerOut* peer, void* stream) {
   if (q_in == nullptr || k_in == nullptr || q_out == nullptr || k_out == nullptr)
     return kErrNullPointer;
   if (hidden != kHidden || batch < 0 || tokens < 0 || heads_per_dest <= 0 ||
@@ -346,6 +365,23 @@ extern "C" int erd_qk_norm_rope(const void* q_in, const void* k_in, const void* 
   p.out_hs = out_head_stride;
   p.out_ds = out_dest_stride;
   p.heads_per_dest = heads_per_dest;
+  p.peer = 0;
+  p.k_rel = p.v_rel = 0;
+  for (int g = 0; g < 16; ++g) p.dest_base[g] = nullptr;
+  if (peer != nullptr) {
+    if (peer->dest_bases == nullptr) return kErrNullPointer;
+    if (peer->ndest != (kHidden / kHeadDimP) / heads_per_dest || peer->ndest > 16)
+      return kErrBadShape;
+    if ((peer->k_rel | peer->v_rel) & 7) return kErrMisaligned;
+    for (int g = 0; g < peer->ndest; ++g) {
+      p.dest_base[g] = static_cast<__nv_bfloat16*>(peer->dest_bases[g]);
+      if (p.dest_base[g] == nullptr) return kErrNullPointer;
+      if (!aligned16(p.dest_base[g])) return kErrMisaligned;
+    }
+    p.k_rel = peer->k_rel;
+    p.v_rel = peer->v_rel;
+    p.peer = 1;
+  }
 
   const long long rows = static_cast<long long>(batch) * tokens;
   const unsigned grid = static_cast<unsigned>((rows + kTokensPerBlock - 1) / kTokensPerBlock);
@@ -356,4 +392,48 @@ extern "C" int erd_qk_norm_rope(const void* q_in, const void* k_in, const void* 
     default: qk_norm_rope_kernel<2><<<grid, kTokensPerBlock * 32, 0, s>>>(p); break;
   }
   return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+extern "C" int erd_qk_norm_rope(const void* q_in, const void* k_in, const void* v_in,
+                                int64_t in_token_stride, int64_t in_batch_stride, int batch,
+                                int tokens, int hidden, const void* q_weight, const void* k_weight,
+                                float eps, int rope_mode, const float* cos_tab,
+                                const float* sin_tab, int64_t tab_token_stride,
+                                int64_t tab_batch_stride, const float* axis_table, int nfreq,
+                                int frames, int height, int width, int token_offset,
+                                const int32_t* grid_index, void* q_out,
+                                void* k_out, void* v_out, int64_t out_token_stride,
+                                int64_t out_batch_stride, int64_t out_head_stride,
+                                int heads_per_dest, int64_t out_dest_stride, void* stream) {
+  return qk_norm_rope_impl(q_in, k_in, v_in, in_token_stride, in_batch_stride, batch, tokens,
+                           hidden, q_weight, k_weight, eps, rope_mode, cos_tab, sin_tab,
+                           tab_token_stride, tab_batch_stride, axis_table, nfreq, frames, height,
+                           width, token_offset, grid_index, q_out, k_out, v_out, out_token_stride,
+                           out_batch_stride, out_head_stride, heads_per_dest, out_dest_stride,
+                           nullptr, stream);
+}
+
+extern "C" int erd_qk_norm_rope_peer(const void* q_in, const void* k_in, const void* v_in,
+                                     int64_t in_token_stride, int64_t in_batch_stride, int batch,
+                                     int tokens, int hidden, const void* q_weight,
+                                     const void* k_weight, float eps, int rope_mode,
+                                     const float* cos_tab, const float* sin_tab,
+                                     int64_t tab_token_stride, int64_t tab_batch_stride,
+                                     const float* axis_table, int nfreq, int frames, int height,
+                                     int width, int token_offset, const int32_t* grid_index,
+                                     void* const* dest_bases, int ndest, int64_t k_offset,
+                                     int64_t v_offset, int64_t out_token_stride,
+                                     int64_t out_batch_stride, int64_t out_head_stride,
+                                     int heads_per_dest, void* stream) {
+  if (dest_bases == nullptr || ndest <= 0) return kErrNullPointer;
+  const PeerOut peer{dest_bases, ndest, k_offset, v_offset};
+  // q_out / k_out only pass the null checks: every store goes through dest_bases.
+  return qk_norm_rope_impl(q_in, k_in, v_in, in_token_stride, in_batch_stride, batch, tokens,
+                           hidden, q_weight, k_weight, eps, rope_mode, cos_tab, sin_tab,
+                           tab_token_stride, tab_batch_stride, axis_table, nfreq, frames, height,
+                           width, token_offset, grid_index, dest_bases[0], dest_bases[0],
+                           v_in != nullptr ? dest_bases[0] : nullptr, out_token_stride,
+                           out_batch_stride, out_head_stride, heads_per_dest, 0, &peer, stream);
 }

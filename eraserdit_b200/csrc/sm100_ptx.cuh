@@ -20,6 +20,8 @@ enum : int {
   kStatusTimeoutMma = 1 << 1,
   kStatusTimeoutSoftmax = 1 << 2,
   kStatusTimeoutEpilogue = 1 << 3,
+  kStatusTimeoutPeer = 1 << 4,  // a peer rank's flag did not arrive in time
+  kStatusPeerFailed = 1 << 5,   // a peer rank signalled a failed phase (negative epoch)
 };
 
 // A wait that has not completed after this many nanoseconds is treated as a

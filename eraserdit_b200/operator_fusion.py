@@ -117,6 +117,30 @@ def qk_norm_rope_into(query, key, q_weight, k_weight, eps, freqs, q_out, k_out,
     _native.check(rc, "erd_qk_norm_rope")
 
 
+def qk_norm_rope_peer_into(query, key, value, q_weight, k_weight, eps, freqs, dest_bases,
+                           k_offset: int, v_offset: int, *, token_offset: int,
+                           out_token_stride: int, out_batch_stride: int, out_head_stride: int,
+                           heads_per_dest: int) -> None:
+    """Enqueue ``erd_qk_norm_rope_peer``: head group g of every token is stored
+    at device address ``dest_bases[g]`` (another rank's receive buffer)."""
+    import ctypes
+    lib = _native.load()
+    batch, tokens, hidden = query.shape
+    if not isinstance(freqs, RopeAxisTable):
+        raise ValueError("the peer prologue takes a RopeAxisTable")
+    bases = (ctypes.c_void_p * len(dest_bases))(*dest_bases)
+    device = query.device
+    with torch.cuda.device(device):
+        rc = lib.erd_qk_norm_rope_peer(
+            query.data_ptr(), key.data_ptr(), _native.ptr(value), query.stride(1),
+            query.stride(0), batch, tokens, hidden, _native.ptr(q_weight), _native.ptr(k_weight),
+            float(eps), 2, None, None, 0, 0, freqs.table.data_ptr(), freqs.nfreq, freqs.frames,
+            freqs.height, freqs.width, int(token_offset), _native.ptr(freqs.grid_index), bases,
+            len(dest_bases), int(k_offset), int(v_offset), out_token_stride, out_batch_stride,
+            out_head_stride, heads_per_dest, _native.stream_handle(device))
+    _native.check(rc, "erd_qk_norm_rope_peer")
+
+
 def apply_fused_qk_rmsnorm_rope(query: torch.Tensor, key: torch.Tensor, query_norm: Any,
                                 key_norm: Any, freqs, *, decision: Any = None,
                                 reference: Any = None) -> tuple[torch.Tensor, torch.Tensor]:

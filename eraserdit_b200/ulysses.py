@@ -38,6 +38,14 @@ chunk c + 1 runs while chunk c attends on the compute stream, and the finished
 chunk c returns while chunk c + 1 attends.  Every rank enqueues the exchanges
 in the same order (in 0, in 1, out 0, in 2, out 1, ...).
 
+With ``transport="peer"`` both exchanges become stores into peer memory over
+NVLink (``peer_exchange.PeerBuffers``, CUDA IPC mappings): the prologue
+writes each head group straight into the destination rank's ``recv1`` slot,
+the attention epilogue writes each output row straight into the token owner's
+``recv2``, and a release/acquire epoch flag per (rank, phase) orders the
+phases (``erd_peer_signal`` / ``erd_peer_wait``, bounded).  No send buffer, no
+NCCL call and no unpacking copy remain on the data path.
+
 With a block-sparse plan (``sparse=``) the sequence is in the plan's tile
 order, ranks own whole 128-token blocks (a floor partition of the blocks), and
 step 4 runs ``erd_attn_fwd_sparse_bf16`` with the plan's lists translated to
@@ -112,7 +120,8 @@ class UlyssesSelfAttention:
 
     def __init__(self, layer: EraserDiTSelfAttention, degree: int, rank: int,
                  exchange: Exchange, group_ranks: tuple[int, ...] | None = None,
-                 sparse=None, head_chunks: int | None = None) -> None:
+                 sparse=None, head_chunks: int | None = None, transport: str = "nccl",
+                 group=None) -> None:
         if layer.heads % degree:
             raise ValueError("attention heads must be divisible by Ulysses degree")
         if degree > 16:
@@ -134,6 +143,15 @@ class UlyssesSelfAttention:
         # A list here collects (start, end) CUDA events around every attention
         # launch on the stream it is enqueued on (for the benchmark's roofline).
         self.attention_events: list | None = None
+        if transport not in ("nccl", "peer"):
+            raise ValueError("transport must be 'nccl' or 'peer'")
+        if transport == "peer" and (layer.precision != "bf16" or sparse is not None
+                                    or (head_chunks or 1) != 1):
+            raise ValueError("the peer transport serves the dense BF16 path with one head chunk")
+        self.transport = transport
+        self.group = group
+        self._peer: dict[tuple, object] = {}
+        self._epoch = 0
 
     def _bounds(self, length: int, rank: int) -> tuple[int, int]:
         if self.sparse is not None:
@@ -283,9 +301,119 @@ class UlyssesSelfAttention:
         attn = heads.permute(3, 2, 1, 0, 4, 5).reshape(b, lme, n * c * hc * HEAD_DIM)
         return self.layer.project_out(attn)
 
+    # ----------------------------------------------------- peer transport
+    def peer_buffers(self, batch: int, length: int, device, connect=True):
+        """This rank's receive buffers for a shape, mapped into the group's
+        ranks (collective over ``group`` on first use)."""
+        from .peer_exchange import PeerBuffers
+        key = (batch, length, str(device))
+        bufs = self._peer.get(key)
+        if bufs is None:
+            lengths = self._lengths(length)
+            hl = self.local_heads
+            sizes = {"recv1": 2 * self.degree * max(lengths) * 3 * batch * hl * HEAD_DIM,
+                     "recv2": 2 * self.degree * lengths[self.rank] * batch * hl * HEAD_DIM}
+            bufs = PeerBuffers(sizes, torch.device(device))
+            if connect:
+                bufs.connect_group(self.group, self.rank, self.degree)
+            self._peer[key] = bufs
+        return bufs
+
+    def close(self) -> None:
+        """Release the peer buffers (after every rank's last call has finished)."""
+        for bufs in self._peer.values():
+            bufs.close()
+        self._peer = {}
+
+    def peer_pre(self, x_local: torch.Tensor, rope, length: int):
+        """QKV projection, then the prologue stores Q/K/V into the peers' recv1."""
+        from .operator_fusion import qk_norm_rope_peer_into
+        from .peer_exchange import PHASE_IN, signal
+        batch = x_local.shape[0]
+        n, hl = self.degree, self.local_heads
+        lengths = self._lengths(length)
+        lmax = max(lengths)
+        start, end = self._bounds(length, self.rank)
+        if x_local.shape[1] != end - start:
+            raise ValueError("local sequence length must match the rank's partition")
+        bufs = self.peer_buffers(batch, length, x_local.device)
+        self._epoch += 1
+        qkv = self.layer.project_qkv(x_local)
+        q, k, v = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN], qkv[..., 2 * HIDDEN:]
+        row1, qkv_gap = 3 * batch * hl * HEAD_DIM, batch * hl * HEAD_DIM
+        # our slot in destination d's recv1[src = this rank][slot token][qkv][b][hl][d]
+        dest = [bufs.peers["recv1"][d] + 2 * self.rank * lmax * row1 for d in range(n)]
+        qk_norm_rope_peer_into(q, k, v, self.layer.norm_q, self.layer.norm_k, self.layer.eps,
+                               rope, dest, qkv_gap, 2 * qkv_gap, token_offset=start,
+                               out_token_stride=row1, out_batch_stride=hl * HEAD_DIM,
+                               out_head_stride=HEAD_DIM, heads_per_dest=hl)
+        stream = _native.stream_handle(x_local.device)
+        signal(bufs, PHASE_IN, self.rank, n, self._epoch, stream)
+        return bufs, lengths, batch
+
+    def peer_attend(self, bufs, lengths, batch) -> bool:
+        """Wait for every rank's Q/K/V, attend, store rows into the owners' recv2."""
+        import ctypes
+        from .peer_exchange import PHASE_IN, PHASE_OUT, signal, wait
+        n, hl = self.degree, self.local_heads
+        lmax = max(lengths)
+        device = bufs.device
+        stream = _native.stream_handle(device)
+        status = _native.status_word(device)
+        wait(bufs, PHASE_IN, n, self._epoch, status, stream)
+        row1, qkv_gap, row2 = 3 * batch * hl * HEAD_DIM, batch * hl * HEAD_DIM, batch * hl * HEAD_DIM
+        base = bufs.local["recv1"]
+        seg_out = (ctypes.c_void_p * n)(*[bufs.peers["recv2"][s] + 2 * self.rank * lengths[s] * row2
+                                          for s in range(n)])
+        lens = (ctypes.c_int32 * n)(*lengths)
+        strides = (row1, HEAD_DIM, hl * HEAD_DIM, lmax * row1)
+        lib = _native.load()
+        events = self.attention_events
+        if events is not None:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        with torch.cuda.device(device):
+            rc = lib.erd_attn_fwd_bf16_peer(
+                base, base + 2 * qkv_gap, base + 4 * qkv_gap, *strides, *strides, *strides, batch,
+                hl, lmax, n, lens, HEAD_DIM, float(self.layer.softmax_scale), seg_out, row2,
+                HEAD_DIM, hl * HEAD_DIM, status.data_ptr(), stream)
+        if events is not None:
+            e1.record()
+            events.append((e0, e1))
+        self.calls += 1
+        # every rank still signals, a failed one with the negative epoch
+        signal(bufs, PHASE_OUT, self.rank, n, self._epoch if rc == 0 else -self._epoch, stream)
+        return rc == 0
+
+    def peer_post(self, bufs, lengths, batch, ok: bool) -> torch.Tensor:
+        """Wait for every rank's rows, check the status, gather heads, project."""
+        from .peer_exchange import PHASE_OUT, wait
+        n, hl = self.degree, self.local_heads
+        device = bufs.device
+        wait(bufs, PHASE_OUT, n, self._epoch, _native.status_word(device),
+             _native.stream_handle(device))
+        status = _native.read_status(device)
+        if not ok:
+            raise RuntimeError("local sequence-parallel attention failed")
+        if status:
+            flags = bufs.view("flags", 32, torch.int32)[16:16 + n].tolist()
+            bad = tuple(self.group_ranks[i] for i, f in enumerate(flags) if f != self._epoch)
+            raise SequenceParallelPeerError(bad or tuple(self.group_ranks))
+        lme = lengths[self.rank]
+        heads = bufs.view("recv2", n * lme * batch * hl * HEAD_DIM, torch.bfloat16)
+        attn = heads.view(n, lme, batch, hl, HEAD_DIM).permute(2, 1, 0, 3, 4)
+        return self.layer.project_out(attn.reshape(batch, lme, n * hl * HEAD_DIM))
+
+    def _forward_peer(self, x_local: torch.Tensor, rope, length: int) -> torch.Tensor:
+        bufs, lengths, batch = self.peer_pre(x_local, rope, length)
+        ok = self.peer_attend(bufs, lengths, batch)
+        return self.peer_post(bufs, lengths, batch, ok)
+
     # -------------------------------------------------------------- forward
     def forward(self, x_local: torch.Tensor, rope, length: int) -> torch.Tensor:
         """Layer output for this rank's tokens [B, L_rank, 2048]."""
+        if self.transport == "peer":
+            return self._forward_peer(x_local, rope, length)
         step = self.pre(x_local, rope, length)
         if step.chunks > 1 and x_local.is_cuda:
             return self._forward_pipelined(step)
@@ -362,14 +490,28 @@ def select_head_chunks(degree: int, length: int, local_heads: int, *, sparse: bo
 
 
 def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, rope,
-                  sparse=None, head_chunks: int | None = None) -> list[torch.Tensor]:
+                  sparse=None, head_chunks: int | None = None, transport: str = "nccl"
+                  ) -> list[torch.Tensor]:
     """Run all ``degree`` ranks of the Ulysses layer inside one process on one
     device, exchanging chunks by copies (the same buffers and kernels as the
     NCCL path).  Returns each rank's output; used to check the data layout on
     a single GPU."""
     length = x.shape[1]
     ranks = [UlyssesSelfAttention(layer, degree, r, exchange=None, sparse=sparse,
-                                  head_chunks=head_chunks) for r in range(degree)]
+                                  head_chunks=head_chunks, transport=transport)
+             for r in range(degree)]
+    if transport == "peer":
+        # every phase of every rank is enqueued before any rank waits on it
+        bufs = [r.peer_buffers(x.shape[0], length, x.device, connect=False) for r in ranks]
+        for b in bufs:
+            b.connect_local(bufs)
+        pre = [r.peer_pre(x[:, r.partition(length)].contiguous(), rope, length) for r in ranks]
+        oks = [r.peer_attend(*args) for r, args in zip(ranks, pre)]
+        outs = [r.peer_post(*args, ok) for r, args, ok in zip(ranks, pre, oks)]
+        torch.cuda.synchronize(x.device)
+        for r in ranks:
+            r.close()
+        return outs
     steps = []
     for r in ranks:
         sl = r.partition(length)

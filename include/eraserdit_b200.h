@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define ERD_ABI_VERSION 2
+#define ERD_ABI_VERSION 3
 
 /* ABI version probe; replaces eraserdit_mask_sta_abi()
  * (layers/attention/backends/csrc/mask_sta/core.cu:767). */
@@ -156,6 +156,66 @@ int erd_gather_tokens(const void* src, int64_t src_token_stride, int64_t src_bat
                       int src_tokens, void* dst, int64_t dst_token_stride,
                       int64_t dst_batch_stride, const int32_t* index, int batch, int tokens,
                       int row_elems, void* stream);
+
+/*
+ * erd_qk_norm_rope with every head group stored straight into another rank's
+ * receive buffer (the input all-to-all of Ulysses SP as peer stores over
+ * NVLink).  Replaces pack_qkv + the first all_to_all_single of
+ * DistributedSequenceRank._ulysses_input (nccl_sequence.py:43-79,
+ * communication_op.py:97-137).  Head group g = head / heads_per_dest goes to
+ * dest_bases[g] (ndest device pointers, CUDA IPC mappings of the peers'
+ * buffers or local memory): Q at +0, K at +k_offset, V at +v_offset elements,
+ * element (b, t, head, d) at + b*out_batch_stride + t*out_token_stride
+ * + (head % heads_per_dest)*out_head_stride + d.  Other arguments as
+ * erd_qk_norm_rope.
+ */
+int erd_qk_norm_rope_peer(const void* q_in, const void* k_in, const void* v_in,
+                          int64_t in_token_stride, int64_t in_batch_stride, int batch, int tokens,
+                          int hidden, const void* q_weight, const void* k_weight, float eps,
+                          int rope_mode, const float* cos_tab, const float* sin_tab,
+                          int64_t tab_token_stride, int64_t tab_batch_stride,
+                          const float* axis_table, int nfreq, int frames, int height, int width,
+                          int token_offset, const int32_t* grid_index, void* const* dest_bases,
+                          int ndest, int64_t k_offset, int64_t v_offset, int64_t out_token_stride,
+                          int64_t out_batch_stride, int64_t out_head_stride, int heads_per_dest,
+                          void* stream);
+
+/*
+ * erd_attn_fwd_bf16 with the output rows of segment s stored at seg_out[s]
+ * (nseg device pointers: the token owners' return buffers, peer or local) +
+ * b*o_batch_stride + h*o_head_stride + t*o_token_stride.  Replaces the second
+ * all-to-all (DistributedSequenceRank._ulysses_output, nccl_sequence.py:81-103).
+ */
+int erd_attn_fwd_bf16_peer(const void* q, const void* k, const void* v, int64_t q_token_stride,
+                           int64_t q_head_stride, int64_t q_batch_stride, int64_t q_seg_stride,
+                           int64_t k_token_stride, int64_t k_head_stride, int64_t k_batch_stride,
+                           int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+                           int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads,
+                           int seg_len, int nseg, const int32_t* seg_lens, int head_dim,
+                           float softmax_scale, void* const* seg_out, int64_t o_token_stride,
+                           int64_t o_head_stride, int64_t o_batch_stride, int* status,
+                           void* stream);
+
+/*
+ * Peer-exchange plumbing (no counterpart entry in the reference, whose
+ * exchange is NCCL's).  erd_peer_alloc is the one allocating entry point: it
+ * cudaMallocs (and zeroes) a buffer that peers map with the 64-byte handle of
+ * erd_peer_ipc_handle / erd_peer_ipc_open (cudaIpcMemLazyEnablePeerAccess).
+ * erd_peer_signal: after the stream's earlier stores, a system-scope fence and
+ * a release store of `epoch` to each of the npeers flag slots (device
+ * pointers, this rank's slot in every rank's flag array).  erd_peer_wait:
+ * acquire loads of n local flags until each equals `epoch`, at most
+ * timeout_ns; on timeout the status word gets 0x10 and the kernel returns.  A
+ * rank whose phase failed signals -epoch: waiters then set 0x20 and return.
+ */
+int erd_peer_alloc(size_t bytes, void** ptr);
+int erd_peer_free(void* ptr);
+int erd_peer_ipc_handle(void* ptr, void* handle64);
+int erd_peer_ipc_open(const void* handle64, void** ptr);
+int erd_peer_ipc_close(void* ptr);
+int erd_peer_signal(int32_t* const* peer_slots, int npeers, int32_t epoch, void* stream);
+int erd_peer_wait(const int32_t* flags, int n, int32_t epoch, int64_t timeout_ns, int* status,
+                  void* stream);
 
 /*
  * SageAttention-style FP8 attention, head_dim 64: K smoothed by its per-head

@@ -56,3 +56,45 @@ def test_head_chunks_bitwise_equal_unchunked(degree, chunks):
     chunked = emulate_ranks(layer, degree, x, rope, head_chunks=chunks)
     for a, b in zip(plain, chunked):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("degree", [2, 4, 8])
+def test_peer_transport_bitwise_equal_nccl_layout(degree):
+    """The peer-memory exchange (prologue and attention epilogue storing into
+    the peers' buffers) gives exactly the all-to-all path's result."""
+    from eraserdit_b200.ulysses import emulate_ranks
+    layer, rope, x = _setup(2, 8, 12, 2, seed=10 + degree)
+    nccl = emulate_ranks(layer, degree, x, rope)
+    peer = emulate_ranks(layer, degree, x, rope, transport="peer")
+    for a, b in zip(nccl, peer):
+        assert torch.equal(a, b)
+
+
+def test_peer_wait_times_out_and_reports_failure():
+    """Failure detection without a GPU fault: a wait on a flag that nothing
+    sets ends after its limit with a status bit; a negative epoch (a failed
+    peer phase) ends it at once with another; the context stays usable."""
+    import time
+    from eraserdit_b200 import _native
+    from eraserdit_b200.peer_exchange import PHASE_IN, PeerBuffers, signal, wait
+    dev = torch.device("cuda", 0)
+    bufs = PeerBuffers({"recv1": 1024, "recv2": 1024}, dev)
+    bufs.connect_local([bufs])
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = _native.stream_handle(dev)
+    t0 = time.perf_counter()
+    wait(bufs, PHASE_IN, 1, 7, status, stream, timeout_ns=50_000_000)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0x10 and time.perf_counter() - t0 < 5
+    status.zero_()
+    signal(bufs, PHASE_IN, 0, 1, -8, stream)
+    wait(bufs, PHASE_IN, 1, 8, status, stream, timeout_ns=2_000_000_000)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0x20
+    status.zero_()
+    signal(bufs, PHASE_IN, 0, 1, 9, stream)
+    wait(bufs, PHASE_IN, 1, 9, status, stream)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert float(torch.ones(4, device=dev).sum()) == 4.0  # the context is fine
+    bufs.close()

@@ -1,6 +1,6 @@
 """Ulysses SP over real NCCL on every visible GPU (skipped with fewer than 2):
-each rank's output equals the single-GPU layer's rows for its tokens, dense
-and block-sparse."""
+each rank's output equals the single-GPU layer's rows for its tokens, dense,
+head-chunked, over peer memory (CUDA IPC) and block-sparse."""
 import os
 import socket
 import tempfile
@@ -52,6 +52,23 @@ def _rank(rank, world, port, out_dir):
                                            ranks, head_chunks=2)
             again = chunked(x[:, sl].contiguous(), rope, x.shape[1])
             assert torch.equal(again, got), "head chunks changed the result"
+        # peer-memory exchange (CUDA IPC mappings, stores over NVLink)
+        rope = LTXVideoRotaryPosEmbed()(2, 8, 12, device=device)
+        g = torch.Generator(device=device).manual_seed(2)
+        x = torch.randn(2, 192, 2048, generator=g, device=device).bfloat16()
+        want = layer(x, rope)
+        sp = UlyssesSelfAttention(layer, world, index, peer_exchange(group, ranks, index), ranks,
+                                  transport="peer", group=group)
+        sl = sp.partition(x.shape[1])
+        for _ in range(3):  # several epochs through the same buffers
+            got = sp(x[:, sl].contiguous(), rope, x.shape[1])
+        err = float((got.float() - want[:, sl].float()).abs().max())
+        cos = float(torch.nn.functional.cosine_similarity(
+            got.float().flatten(), want[:, sl].float().flatten(), dim=0))
+        assert err <= 1e-2 and cos >= 0.99999, ("peer", err, cos)
+        torch.cuda.synchronize()
+        dist.barrier()
+        sp.close()
         # block-sparse attention over the exchange (whole 128-token blocks per rank)
         from eraserdit_b200 import sparse_pattern as sp_pattern
         from eraserdit_b200.mask_sta import SparsePlan
