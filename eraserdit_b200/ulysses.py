@@ -152,6 +152,11 @@ class UlyssesSelfAttention:
         self.group = group
         self._peer: dict[tuple, object] = {}
         self._epoch = 0
+        # Peer transport: a call's status word is copied to pinned host memory
+        # on the stream and inspected at the next call (or in drain()), so
+        # that no host synchronisation sits between consecutive layers.
+        self._pending = None
+        self._status_host = None
 
     def _bounds(self, length: int, rank: int) -> tuple[int, int]:
         if self.sparse is not None:
@@ -319,11 +324,27 @@ class UlyssesSelfAttention:
             self._peer[key] = bufs
         return bufs
 
+    def drain(self) -> None:
+        """Raise the error of the last peer-transport call, if it had one."""
+        pending, self._pending = self._pending, None
+        if pending is None:
+            return
+        event, host, bufs, epoch, n = pending
+        event.synchronize()
+        status = int(host[0])
+        if status:
+            flags = bufs.view("flags", 32, torch.int32)[16:16 + n].tolist()
+            bad = tuple(self.group_ranks[i] for i, f in enumerate(flags) if f != epoch)
+            raise SequenceParallelPeerError(bad or tuple(self.group_ranks))
+
     def close(self) -> None:
         """Release the peer buffers (after every rank's last call has finished)."""
-        for bufs in self._peer.values():
-            bufs.close()
-        self._peer = {}
+        try:
+            self.drain()
+        finally:
+            for bufs in self._peer.values():
+                bufs.close()
+            self._peer = {}
 
     def peer_pre(self, x_local: torch.Tensor, rope, length: int):
         """QKV projection, then the prologue stores Q/K/V into the peers' recv1."""
@@ -390,21 +411,26 @@ class UlyssesSelfAttention:
         from .peer_exchange import PHASE_OUT, wait
         n, hl = self.degree, self.local_heads
         device = bufs.device
-        wait(bufs, PHASE_OUT, n, self._epoch, _native.status_word(device),
-             _native.stream_handle(device))
-        status = _native.read_status(device)
+        word = _native.status_word(device)
+        wait(bufs, PHASE_OUT, n, self._epoch, word, _native.stream_handle(device))
         if not ok:
             raise RuntimeError("local sequence-parallel attention failed")
-        if status:
-            flags = bufs.view("flags", 32, torch.int32)[16:16 + n].tolist()
-            bad = tuple(self.group_ranks[i] for i, f in enumerate(flags) if f != self._epoch)
-            raise SequenceParallelPeerError(bad or tuple(self.group_ranks))
+        # status of this call: to pinned host memory now, inspected by drain()
+        if getattr(self, "_status_host", None) is None:
+            self._status_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+        host = self._status_host  # free again: drain() ran at the start of this call
+        host.copy_(word, non_blocking=True)
+        word.zero_()
+        event = torch.cuda.Event()
+        event.record()
+        self._pending = (event, host, bufs, self._epoch, n)
         lme = lengths[self.rank]
         heads = bufs.view("recv2", n * lme * batch * hl * HEAD_DIM, torch.bfloat16)
         attn = heads.view(n, lme, batch, hl, HEAD_DIM).permute(2, 1, 0, 3, 4)
         return self.layer.project_out(attn.reshape(batch, lme, n * hl * HEAD_DIM))
 
     def _forward_peer(self, x_local: torch.Tensor, rope, length: int) -> torch.Tensor:
+        self.drain()  # the previous call's status (normally complete by now)
         bufs, lengths, batch = self.peer_pre(x_local, rope, length)
         ok = self.peer_attend(bufs, lengths, batch)
         return self.peer_post(bufs, lengths, batch, ok)
@@ -510,7 +536,7 @@ def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, r
         outs = [r.peer_post(*args, ok) for r, args, ok in zip(ranks, pre, oks)]
         torch.cuda.synchronize(x.device)
         for r in ranks:
-            r.close()
+            r.close()  # raises a failed peer's error
         return outs
     steps = []
     for r in ranks:

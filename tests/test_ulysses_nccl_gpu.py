@@ -68,7 +68,7 @@ def _rank(rank, world, port, out_dir):
         assert err <= 1e-2 and cos >= 0.99999, ("peer", err, cos)
         torch.cuda.synchronize()
         dist.barrier()
-        sp.close()
+        sp.close()  # raises if any call of this object saw a peer error
         # block-sparse attention over the exchange (whole 128-token blocks per rank)
         from eraserdit_b200 import sparse_pattern as sp_pattern
         from eraserdit_b200.mask_sta import SparsePlan
