@@ -51,9 +51,6 @@ struct PrologueParams {
   int peer;
 };
 
-__device__ __forceinline__ float bf16_round(float x) {
-  return __bfloat162float(__float2bfloat16_rn(x));
-}
 
 __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -64,15 +61,22 @@ __device__ __forceinline__ void unpack8(const uint4& v, float (&f)[8]) {
   }
 }
 
+// Two values rounded to BF16 (nearest even) by one packed conversion.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ void bf16_round2(float& a, float& b) {
+  const uint32_t r = cvt_bf16x2(a, b);
+  a = __uint_as_float(r << 16);
+  b = __uint_as_float(r & 0xFFFF0000u);
+}
+
 __device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i]));
-    const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i + 1]));
-    w[i] = lo | (hi << 16);
-  }
-  return make_uint4(w[0], w[1], w[2], w[3]);
+  return make_uint4(cvt_bf16x2(f[0], f[1]), cvt_bf16x2(f[2], f[3]), cvt_bf16x2(f[4], f[5]),
+                    cvt_bf16x2(f[6], f[7]));
 }
 
 // y = bf16(x * r), then z = bf16(y * w) when an affine weight is present.
@@ -82,10 +86,16 @@ __device__ __forceinline__ void norm8(float (&x)[8], float r, const __nv_bfloat1
     unpack8(__ldg(reinterpret_cast<const uint4*>(w + c0)), wf);
   }
 #pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    float y = bf16_round(__fmul_rn(x[e], r));
-    if (w != nullptr) y = bf16_round(__fmul_rn(y, wf[e]));
-    x[e] = y;
+  for (int e = 0; e < 8; e += 2) {
+    float y0 = __fmul_rn(x[e], r), y1 = __fmul_rn(x[e + 1], r);
+    bf16_round2(y0, y1);
+    if (w != nullptr) {
+      y0 = __fmul_rn(y0, wf[e]);
+      y1 = __fmul_rn(y1, wf[e + 1]);
+      bf16_round2(y0, y1);
+    }
+    x[e] = y0;
+    x[e + 1] = y1;
   }
 }
 
@@ -140,17 +150,20 @@ __global__ void __launch_bounds__(kTokensPerBlock * 32, 3)
 
   // fp32 sum of squares over the full 2048-wide rows (squares of BF16 values
   // are exact in fp32).
-  float sq = 0.f, sk = 0.f;
+  // Four partial sums per lane keep the dependent-add chains short.
+  float sq4[4] = {0.f, 0.f, 0.f, 0.f}, sk4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int it = 0; it < kChunksPerLane; ++it) {
     float f[8];
     unpack8(qv[it], f);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sq = __fadd_rn(sq, __fmul_rn(f[e], f[e]));
+    for (int e = 0; e < 8; ++e) sq4[e & 3] = __fmaf_rn(f[e], f[e], sq4[e & 3]);
     unpack8(kv[it], f);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sk = __fadd_rn(sk, __fmul_rn(f[e], f[e]));
+    for (int e = 0; e < 8; ++e) sk4[e & 3] = __fmaf_rn(f[e], f[e], sk4[e & 3]);
   }
+  float sq = (sq4[0] + sq4[1]) + (sq4[2] + sq4[3]);
+  float sk = (sk4[0] + sk4[1]) + (sk4[2] + sk4[3]);
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) {
     sq += __shfl_xor_sync(0xffffffffu, sq, off);
