@@ -50,8 +50,7 @@ def run_sequence_parallel(args) -> None:
         x_full = torch.randn(B.BATCH, B.SEQ, B.HIDDEN, generator=g, device=device).bfloat16()
         per_branch = B.BATCH // cfg
         x_branch = x_full[cfg_index * per_branch:(cfg_index + 1) * per_branch]
-        # The peer transport serves the dense BF16 path; FP8 and sparse use NCCL.
-        transport = args.transport if not (args.fp8 or args.sparse) else "nccl"
+        transport = args.transport
         sp = UlyssesSelfAttention(layer, len(ranks), index, peer_exchange(group, ranks, index),
                                   group_ranks=ranks, sparse=plan, head_chunks=args.head_chunks,
                                   transport=transport, group=group)

@@ -652,3 +652,37 @@ extern "C" int erd_attn_fwd_bf16_peer(
   for (int s = 0; s < nseg; ++s) L.p.seg_out[s] = static_cast<__nv_bfloat16*>(seg_out[s]);
   return launch<false>(L, static_cast<unsigned>((L.p.q_tiles + 1) / 2), heads, batch, stream);
 }
+
+extern "C" int erd_attn_fwd_sparse_bf16_peer(
+    const void* q, const void* k, const void* v, int64_t q_token_stride, int64_t q_head_stride,
+    int64_t q_batch_stride, int64_t q_seg_stride, int64_t k_token_stride, int64_t k_head_stride,
+    int64_t k_batch_stride, int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+    int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads, int seg_len, int nseg,
+    const int32_t* seg_lens, int head_dim, float softmax_scale, void* const* seg_out,
+    int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride,
+    const int32_t* schedule, int n_schedule, const uint32_t* entries, int64_t n_entries,
+    int* status, void* stream) {
+  if (seg_out == nullptr || schedule == nullptr || entries == nullptr) return kErrNullPointer;
+  if (nseg <= 0 || nseg > kMaxSegments || n_schedule <= 0 || n_schedule > (1 << 30) ||
+      n_entries <= 0)
+    return kErrBadShape;
+  for (int s = 0; s < nseg; ++s) {
+    if (seg_out[s] == nullptr) return kErrNullPointer;
+    if (!aligned16(seg_out[s])) return kErrMisaligned;
+  }
+  if ((reinterpret_cast<uintptr_t>(schedule) & 15) != 0 ||
+      (reinterpret_cast<uintptr_t>(entries) & 3) != 0)
+    return kErrMisaligned;
+  Launch L;
+  if (int rc = prepare(q, k, v, q_token_stride, q_head_stride, q_batch_stride, q_seg_stride,
+                       k_token_stride, k_head_stride, k_batch_stride, k_seg_stride,
+                       v_token_stride, v_head_stride, v_batch_stride, v_seg_stride, batch, heads,
+                       seg_len, nseg, seg_lens, head_dim, softmax_scale, seg_out[0],
+                       o_token_stride, o_head_stride, o_batch_stride, 0, status, &L))
+    return rc;
+  L.p.sched = reinterpret_cast<const int4*>(schedule);
+  L.p.entries = entries;
+  L.p.n_entries = n_entries;
+  for (int s = 0; s < nseg; ++s) L.p.seg_out[s] = static_cast<__nv_bfloat16*>(seg_out[s]);
+  return launch<true>(L, static_cast<unsigned>(n_schedule), heads, batch, stream);
+}

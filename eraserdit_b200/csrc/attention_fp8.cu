@@ -273,6 +273,9 @@ struct AttnParams {
   __nv_bfloat16* out;
   Layout lo;
   int* status;
+  // Optional per-segment output bases (another rank's return buffer); when set
+  // they replace out + segment * lo.ss.
+  __nv_bfloat16* seg_out[kMaxSegments];
 };
 
 struct __align__(8) Barriers {
@@ -568,8 +571,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (tok < p.g.seg_lens[seg]) {
           const float inv = kStaleScale / (l_run * kE4M3Max);
           const float* sv = p.sv + static_cast<size_t>(bh) * kDim;
-          __nv_bfloat16* dst =
-              p.out + seg * p.lo.ss + batch * p.lo.bs + head * p.lo.hs + tok * p.lo.ts;
+          __nv_bfloat16* seg_base = p.seg_out[seg] != nullptr ? p.seg_out[seg] : p.out + seg * p.lo.ss;
+          __nv_bfloat16* dst = seg_base + batch * p.lo.bs + head * p.lo.hs + tok * p.lo.ts;
 #pragma unroll
           for (int v = 0; v < 8; ++v) {
             float f[8];
@@ -640,18 +643,18 @@ extern "C" size_t erd_attn_fp8_workspace_bytes(int batch, int heads, int seg_len
   return fp8::workspace_layout(batch, heads, tiles, nullptr, nullptr);
 }
 
-extern "C" int erd_attn_fwd_fp8(const void* q, const void* k, const void* v,
-                                int64_t q_token_stride, int64_t q_head_stride,
-                                int64_t q_batch_stride, int64_t q_seg_stride,
-                                int64_t k_token_stride, int64_t k_head_stride,
-                                int64_t k_batch_stride, int64_t k_seg_stride,
-                                int64_t v_token_stride, int64_t v_head_stride,
-                                int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads,
-                                int seg_len, int nseg, const int32_t* seg_lens, int head_dim,
-                                float softmax_scale, void* out, int64_t o_token_stride,
-                                int64_t o_head_stride, int64_t o_batch_stride,
-                                int64_t o_seg_stride, void* workspace, size_t workspace_bytes,
-                                int* status, void* stream) {
+namespace {
+
+int attn_fwd_fp8_impl(const void* q, const void* k, const void* v, int64_t q_token_stride,
+                      int64_t q_head_stride, int64_t q_batch_stride, int64_t q_seg_stride,
+                      int64_t k_token_stride, int64_t k_head_stride, int64_t k_batch_stride,
+                      int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+                      int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads,
+                      int seg_len, int nseg, const int32_t* seg_lens, int head_dim,
+                      float softmax_scale, void* out, int64_t o_token_stride,
+                      int64_t o_head_stride, int64_t o_batch_stride, int64_t o_seg_stride,
+                      void* const* seg_out, void* workspace, size_t workspace_bytes,
+                      int* status, void* stream) {
   if (q == nullptr || k == nullptr || v == nullptr || out == nullptr || workspace == nullptr)
     return kErrNullPointer;
   if (head_dim != fp8::kDim) return kErrBadShape;
@@ -715,6 +718,9 @@ extern "C" int erd_attn_fwd_fp8(const void* q, const void* k, const void* v,
   p.out = static_cast<__nv_bfloat16*>(out);
   p.lo = fp8::Layout{o_token_stride, o_head_stride, o_batch_stride, o_seg_stride};
   p.status = status;
+  for (int s = 0; s < fp8::kMaxSegments; ++s)
+    p.seg_out[s] = (seg_out != nullptr && s < nseg) ? static_cast<__nv_bfloat16*>(seg_out[s])
+                                                     : nullptr;
   e = cudaFuncSetAttribute(fp8::attn_fwd_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            fp8::kSmemLaunchBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
@@ -722,4 +728,48 @@ extern "C" int erd_attn_fwd_fp8(const void* q, const void* k, const void* v,
                   static_cast<unsigned>(batch));
   fp8::attn_fwd_fp8_kernel<<<grid, fp8::kThreads, fp8::kSmemLaunchBytes, s>>>(tq, tk, tv, p);
   return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+extern "C" int erd_attn_fwd_fp8(const void* q, const void* k, const void* v,
+                                int64_t q_token_stride, int64_t q_head_stride,
+                                int64_t q_batch_stride, int64_t q_seg_stride,
+                                int64_t k_token_stride, int64_t k_head_stride,
+                                int64_t k_batch_stride, int64_t k_seg_stride,
+                                int64_t v_token_stride, int64_t v_head_stride,
+                                int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads,
+                                int seg_len, int nseg, const int32_t* seg_lens, int head_dim,
+                                float softmax_scale, void* out, int64_t o_token_stride,
+                                int64_t o_head_stride, int64_t o_batch_stride,
+                                int64_t o_seg_stride, void* workspace, size_t workspace_bytes,
+                                int* status, void* stream) {
+  return attn_fwd_fp8_impl(q, k, v, q_token_stride, q_head_stride, q_batch_stride, q_seg_stride,
+                           k_token_stride, k_head_stride, k_batch_stride, k_seg_stride,
+                           v_token_stride, v_head_stride, v_batch_stride, v_seg_stride, batch,
+                           heads, seg_len, nseg, seg_lens, head_dim, softmax_scale, out,
+                           o_token_stride, o_head_stride, o_batch_stride, o_seg_stride, nullptr,
+                           workspace, workspace_bytes, status, stream);
+}
+
+extern "C" int erd_attn_fwd_fp8_peer(
+    const void* q, const void* k, const void* v, int64_t q_token_stride, int64_t q_head_stride,
+    int64_t q_batch_stride, int64_t q_seg_stride, int64_t k_token_stride, int64_t k_head_stride,
+    int64_t k_batch_stride, int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+    int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads, int seg_len, int nseg,
+    const int32_t* seg_lens, int head_dim, float softmax_scale, void* const* seg_out,
+    int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride, void* workspace,
+    size_t workspace_bytes, int* status, void* stream) {
+  if (seg_out == nullptr) return kErrNullPointer;
+  if (nseg <= 0 || nseg > fp8::kMaxSegments) return kErrBadShape;
+  for (int s = 0; s < nseg; ++s) {
+    if (seg_out[s] == nullptr) return kErrNullPointer;
+    if (!aligned16(seg_out[s])) return kErrMisaligned;
+  }
+  return attn_fwd_fp8_impl(q, k, v, q_token_stride, q_head_stride, q_batch_stride, q_seg_stride,
+                           k_token_stride, k_head_stride, k_batch_stride, k_seg_stride,
+                           v_token_stride, v_head_stride, v_batch_stride, v_seg_stride, batch,
+                           heads, seg_len, nseg, seg_lens, head_dim, softmax_scale, seg_out[0],
+                           o_token_stride, o_head_stride, o_batch_stride, 0, seg_out, workspace,
+                           workspace_bytes, status, stream);
 }

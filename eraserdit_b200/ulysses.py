@@ -145,9 +145,8 @@ class UlyssesSelfAttention:
         self.attention_events: list | None = None
         if transport not in ("nccl", "peer"):
             raise ValueError("transport must be 'nccl' or 'peer'")
-        if transport == "peer" and (layer.precision != "bf16" or sparse is not None
-                                    or (head_chunks or 1) != 1):
-            raise ValueError("the peer transport serves the dense BF16 path with one head chunk")
+        if transport == "peer" and (head_chunks or 1) != 1:
+            raise ValueError("the peer transport exchanges all heads at once (one head chunk)")
         self.transport = transport
         self.group = group
         self._peer: dict[tuple, object] = {}
@@ -358,6 +357,9 @@ class UlyssesSelfAttention:
         if x_local.shape[1] != end - start:
             raise ValueError("local sequence length must match the rank's partition")
         bufs = self.peer_buffers(batch, length, x_local.device)
+        if (self.sparse is not None and isinstance(rope, RopeAxisTable)
+                and rope.grid_index is None):
+            rope = rope.in_order(self.sparse.order)
         self._epoch += 1
         qkv = self.layer.project_qkv(x_local)
         q, k, v = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN], qkv[..., 2 * HIDDEN:]
@@ -393,11 +395,23 @@ class UlyssesSelfAttention:
         if events is not None:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
+        common = (base, base + 2 * qkv_gap, base + 4 * qkv_gap, *strides, *strides, *strides,
+                  batch, hl, lmax, n, lens, HEAD_DIM, float(self.layer.softmax_scale), seg_out,
+                  row2, HEAD_DIM, hl * HEAD_DIM)
         with torch.cuda.device(device):
-            rc = lib.erd_attn_fwd_bf16_peer(
-                base, base + 2 * qkv_gap, base + 4 * qkv_gap, *strides, *strides, *strides, batch,
-                hl, lmax, n, lens, HEAD_DIM, float(self.layer.softmax_scale), seg_out, row2,
-                HEAD_DIM, hl * HEAD_DIM, status.data_ptr(), stream)
+            if self.sparse is not None:
+                plan = self._sparse_segments.get(sum(lengths))  # keyed by sequence length
+                if plan is None:
+                    plan = self.sparse.for_segments([l // 128 for l in lengths], lmax // 128)
+                    self._sparse_segments[sum(lengths)] = plan
+                rc = lib.erd_attn_fwd_sparse_bf16_peer(*common, *plan.launch_args(),
+                                                       status.data_ptr(), stream)
+            elif self.layer.precision == "fp8":
+                from .attention import fp8_workspace
+                ws, ws_bytes = fp8_workspace(device, batch, hl, lmax, n)
+                rc = lib.erd_attn_fwd_fp8_peer(*common, ws, ws_bytes, status.data_ptr(), stream)
+            else:
+                rc = lib.erd_attn_fwd_bf16_peer(*common, status.data_ptr(), stream)
         if events is not None:
             e1.record()
             events.append((e0, e1))

@@ -197,6 +197,31 @@ int erd_attn_fwd_bf16_peer(const void* q, const void* k, const void* v, int64_t 
                            void* stream);
 
 /*
+ * The block-sparse and FP8 attentions with the same per-segment output
+ * pointers (erd_attn_fwd_sparse_bf16 / erd_attn_fwd_fp8 arguments otherwise;
+ * out and o_seg_stride replaced by seg_out).
+ */
+int erd_attn_fwd_sparse_bf16_peer(
+    const void* q, const void* k, const void* v, int64_t q_token_stride, int64_t q_head_stride,
+    int64_t q_batch_stride, int64_t q_seg_stride, int64_t k_token_stride, int64_t k_head_stride,
+    int64_t k_batch_stride, int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+    int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads, int seg_len, int nseg,
+    const int32_t* seg_lens, int head_dim, float softmax_scale, void* const* seg_out,
+    int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride,
+    const int32_t* schedule, int n_schedule, const uint32_t* entries, int64_t n_entries,
+    int* status, void* stream);
+
+int erd_attn_fwd_fp8_peer(const void* q, const void* k, const void* v, int64_t q_token_stride,
+                          int64_t q_head_stride, int64_t q_batch_stride, int64_t q_seg_stride,
+                          int64_t k_token_stride, int64_t k_head_stride, int64_t k_batch_stride,
+                          int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+                          int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads,
+                          int seg_len, int nseg, const int32_t* seg_lens, int head_dim,
+                          float softmax_scale, void* const* seg_out, int64_t o_token_stride,
+                          int64_t o_head_stride, int64_t o_batch_stride, void* workspace,
+                          size_t workspace_bytes, int* status, void* stream);
+
+/*
  * Peer-exchange plumbing (no counterpart entry in the reference, whose
  * exchange is NCCL's).  erd_peer_alloc is the one allocating entry point: it
  * cudaMallocs (and zeroes) a buffer that peers map with the 64-byte handle of

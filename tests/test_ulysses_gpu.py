@@ -98,3 +98,31 @@ def test_peer_wait_times_out_and_reports_failure():
     assert int(status.item()) == 0
     assert float(torch.ones(4, device=dev).sum()) == 4.0  # the context is fine
     bufs.close()
+
+
+@pytest.mark.parametrize("degree,kind", [(4, "fp8"), (8, "sparse")])
+def test_peer_transport_fp8_and_sparse(degree, kind):
+    """FP8 and block-sparse attention over the peer-memory exchange: the same
+    result as their all-to-all path."""
+    from eraserdit_b200 import sparse_pattern as sp
+    from eraserdit_b200.layer import EraserDiTSelfAttention
+    from eraserdit_b200.mask_sta import SparsePlan
+    from eraserdit_b200.rotary import LTXVideoRotaryPosEmbed
+    from eraserdit_b200.ulysses import emulate_ranks
+    p = make_params(21, 1e-6, device="cuda")
+    if kind == "fp8":
+        layer = EraserDiTSelfAttention.from_params(p.to(torch.bfloat16), device="cuda",
+                                                   precision="fp8")
+        grid, plan = (2, 8, 12), None
+    else:
+        layer = EraserDiTSelfAttention.from_params(p.to(torch.bfloat16), device="cuda")
+        geom = sp.StaGeometry(grid=(8, 16, 32), window=(1, 3, 2), kv_block=128)
+        grid = geom.grid
+        plan = SparsePlan.from_mask(sp.ellipse_masks(grid, seed=4, semi_axes=(2, 4)), geom, "cuda")
+    rope = LTXVideoRotaryPosEmbed()(*grid)
+    g = torch.Generator(device="cuda").manual_seed(22)
+    x = torch.randn(2, grid[0] * grid[1] * grid[2], 2048, generator=g, device="cuda").bfloat16()
+    nccl = emulate_ranks(layer, degree, x, rope, sparse=plan)
+    peer = emulate_ranks(layer, degree, x, rope, sparse=plan, transport="peer")
+    for a, b in zip(nccl, peer):
+        assert torch.equal(a, b)
