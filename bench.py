@@ -265,6 +265,13 @@ SPARSE_WORKLOAD = ("config 4: mask-aware block-sparse self-attention layer, B=2 
                    "window rounded out to tiles; BF16")
 
 
+def enable_qkv_fp8(layer, x) -> None:
+    """FP8 shared QKV with the activation scale calibrated on the input (amax / 448)."""
+    from eraserdit_b200.synthetic import make_params
+    p = make_params(1, EPS, device=x.device).to(torch.bfloat16)
+    layer.enable_qkv_fp8(float(x.float().abs().amax()) / 448, p.wq, p.bq, p.wk, p.bk, p.wv, p.bv)
+
+
 def build_sparse_plan(device):
     """Configuration 4's pattern; returns (plan, kept fraction, issued fraction)."""
     from eraserdit_b200 import sparse_pattern as sp
@@ -317,6 +324,8 @@ def run_single(args) -> None:
         rope = rope.in_order(plan.order)  # the sequence is laid out in tile order
     g = torch.Generator(device=device).manual_seed(1)
     x = torch.randn(BATCH, SEQ, HIDDEN, generator=g, device=device).bfloat16()
+    if args.qkv_fp8:
+        enable_qkv_fp8(layer, x)
     stream = torch.cuda.current_stream(device)
     attn_events = []
 
@@ -390,11 +399,13 @@ def run_single(args) -> None:
         kernel = "attn_fwd_fp8 (+ fp8 quantize)"
     else:
         workload, kernel = WORKLOAD, "attn_fwd_bf16"
+    if args.qkv_fp8:
+        workload += ", FP8 shared QKV projection (E4M3, static activation scale)"
     line = {
         "metric": METRIC, "value": layer_flop / (ms / 1e3) / 1e12, "unit": UNIT, "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "e4m3/bf16" if args.fp8 else "bf16", "data": "synthetic",
+        "dtype": "e4m3/bf16" if (args.fp8 or args.qkv_fp8) else "bf16", "data": "synthetic",
         "config": {"workload": workload,
                    "global_batch": BATCH, "seq_len": SEQ, "parallelism": "sp1",
                    "l2": "inputs larger than L2 (x 267 MB, QKV 802 MB per step)"},
@@ -411,7 +422,7 @@ def run_single(args) -> None:
                 "h2d_bytes_per_step": host_x.numel() * host_x.element_size(),
                 "d2h_bytes_per_step": host_y[0].numel() * host_y[0].element_size(),
                 "streams": 2},
-        "gpu_launches": (4 if args.fp8 else 2) * args.steps,
+        "gpu_launches": ((4 if args.fp8 else 2) + (1 if args.qkv_fp8 else 0)) * args.steps,
         "clocks": clock,
     }
     if plan is not None:
@@ -435,6 +446,8 @@ def main() -> None:
                         help="Sage-style FP8 attention (configuration 3) instead of BF16")
     parser.add_argument("--sparse", action="store_true",
                         help="mask-aware block-sparse attention (configuration 4)")
+    parser.add_argument("--qkv-fp8", action="store_true",
+                        help="FP8 shared QKV projection (static activation scale)")
     parser.add_argument("--transport", default="peer", choices=["peer", "nccl"],
                         help="Ulysses exchange: peer-memory stores over NVLink or NCCL all-to-all")
     parser.add_argument("--head-chunks", type=int, default=None,

@@ -59,6 +59,12 @@ class EraserDiTSelfAttention:
         if precision not in ("bf16", "fp8"):
             raise ValueError("precision must be bf16 or fp8")
         self.precision = precision
+        self.qkv_fp8 = None  # optional SharedQKV (FP8 projection, static activation scale)
+
+    def enable_qkv_fp8(self, activation_scale: float, wq, bq, wk, bk, wv, bv) -> None:
+        """Project Q|K|V with the FP8 shared QKV GEMM (``qkv_fp8.SharedQKV``)."""
+        from .qkv_fp8 import SharedQKV
+        self.qkv_fp8 = SharedQKV(wq, bq, wk, bk, wv, bv, activation_scale, self.device)
 
     @classmethod
     def from_params(cls, p, device="cuda", precision: str = "bf16") -> "EraserDiTSelfAttention":
@@ -75,6 +81,8 @@ class EraserDiTSelfAttention:
                    attn.norm_q.eps, heads=attn.heads, device=device)
 
     def project_qkv(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        if self.qkv_fp8 is not None:
+            return self.qkv_fp8.project(hidden_states)
         return F.linear(hidden_states, self.w_qkv, self.b_qkv)
 
     def core(self, qkv: torch.Tensor, rope, out: torch.Tensor | None = None,

@@ -243,6 +243,15 @@ int erd_peer_wait(const int32_t* flags, int n, int32_t epoch, int64_t timeout_ns
                   void* stream);
 
 /*
+ * Static-scale E4M3 quantisation of n BF16 values (n a multiple of 16):
+ * out[i] = E4M3_RN(clamp(x[i] / scale, -448, 448)) with an IEEE division.
+ * Replaces the activation quantiser of SharedQKV
+ * (layers/quantization/qkv_fp8.py:52-55; _quant_fp8_tensor,
+ * layers/quantization/eraserdit_fp8.py:60-69).
+ */
+int erd_quantize_e4m3(const void* x, void* out, int64_t n, float scale, void* stream);
+
+/*
  * SageAttention-style FP8 attention, head_dim 64: K smoothed by its per-head
  * token mean, Q and K quantised to E4M3 per 128-token block, V to E4M3 per
  * channel, P to E4M3 (scaled by 448), FP32 accumulation (tcgen05
