@@ -61,6 +61,7 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only if max gr
 constexpr int kPolyPairsPer8 = ERD_POLY_EVERY8;
 
 constexpr int kMaxSegments = 16;
+constexpr int kMaxCrossBatch = 16;  // batch entries with their own key count (cross-attention)
 
 struct AttnParams {
   int seg_lens[kMaxSegments];  // tokens of each segment (<= seg_len, the slot length)
@@ -80,6 +81,12 @@ struct AttnParams {
   // Optional per-segment output bases (another rank's return buffer); when set
   // they replace out + segment * o_ss.
   __nv_bfloat16* seg_out[kMaxSegments];
+  // Key / value tiling: the query tiling for self-attention; its own length for
+  // cross-attention, where kv_valid[batch] (kv_per_batch != 0) counts the
+  // attended keys of each batch entry (the text mask's unpadded prefix).
+  int kv_tiles, kv_tiles_per_seg;
+  int kv_per_batch;
+  int kv_valid[kMaxCrossBatch];
 };
 
 constexpr uint32_t kEntryTileMask = (1u << 24) - 1;
@@ -132,7 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // Query tiles of the two softmax warpgroups and the key tiles to visit: all
   // of them (the same tiling is used for keys and queries), or a list.
   int q_tile_a = 2 * static_cast<int>(blockIdx.x), q_tile_b = q_tile_a + 1;
-  int n_kv = p.q_tiles;
+  int n_kv = p.kv_tiles;
   const uint32_t* list = nullptr;
   if (kSparse) {
     const int4 row = p.sched[blockIdx.x];
@@ -194,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Key tiles past the last one read as zeros (TMA fills out-of-range
         // boxes) and are masked by the softmax.
         const int kv = kSparse ? static_cast<int>(__ldg(list + j) & kEntryTileMask) : j;
-        tile_coords(kv, p.tiles_per_seg, seg, l0);
+        tile_coords(kv, p.kv_tiles_per_seg, seg, l0);
         if (!mbar_wait(smem_u32(&bars->k_empty[s]), ph ^ 1, abort, p.status,
                        kStatusTimeoutProducer))
           break;
@@ -319,17 +326,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kv = static_cast<int>(entry & kEntryTileMask);
         const uint32_t halves = (entry >> (24 + 2 * t)) & 3u;
         hi = 0;
-        if (halves != 0 && kv < p.q_tiles) {
+        if (halves != 0 && kv < p.kv_tiles) {
           int seg, l0;
-          tile_coords(kv, p.tiles_per_seg, seg, l0);
-          hi = min(kBlockN, p.seg_lens[seg] - l0);
+          tile_coords(kv, p.kv_tiles_per_seg, seg, l0);
+          hi = min(kBlockN, (p.kv_per_batch ? p.kv_valid[batch] : p.seg_lens[seg]) - l0);
           if (!(halves & 2u)) hi = min(hi, kBlockN / 2);
           if (!(halves & 1u)) lo = kBlockN / 2;
         }
       } else {
         int seg, l0;
-        tile_coords(j, p.tiles_per_seg, seg, l0);
-        hi = min(kBlockN, p.seg_lens[seg] - l0);
+        tile_coords(j, p.kv_tiles_per_seg, seg, l0);
+        hi = min(kBlockN, (p.kv_per_batch ? p.kv_valid[batch] : p.seg_lens[seg]) - l0);
       }
       // Pass 1: row max over the whole S row (registers released afterwards).
       // A key tile this query tile does not attend at all (sparse lists only)
@@ -559,6 +566,10 @@ int prepare(const void* q, const void* k, const void* v, int64_t q_token_stride,
   p.n_entries = 0;
   p.out_rows = nullptr;
   for (int s = 0; s < kMaxSegments; ++s) p.seg_out[s] = nullptr;
+  p.kv_tiles = p.q_tiles;
+  p.kv_tiles_per_seg = tiles_per_seg;
+  p.kv_per_batch = 0;
+  for (int b = 0; b < kMaxCrossBatch; ++b) p.kv_valid[b] = 0;
   return kErrOk;
 }
 
@@ -685,4 +696,44 @@ extern "C" int erd_attn_fwd_sparse_bf16_peer(
   L.p.n_entries = n_entries;
   for (int s = 0; s < nseg; ++s) L.p.seg_out[s] = static_cast<__nv_bfloat16*>(seg_out[s]);
   return launch<true>(L, static_cast<unsigned>(n_schedule), heads, batch, stream);
+}
+
+extern "C" int erd_attn_fwd_cross_bf16(
+    const void* q, const void* k, const void* v, int64_t q_token_stride, int64_t q_head_stride,
+    int64_t q_batch_stride, int64_t k_token_stride, int64_t k_head_stride, int64_t k_batch_stride,
+    int64_t v_token_stride, int64_t v_head_stride, int64_t v_batch_stride, int batch, int heads,
+    int q_len, int kv_len, const int32_t* kv_valid, int head_dim, float softmax_scale, void* out,
+    int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride, int* status,
+    void* stream) {
+  if (q == nullptr || k == nullptr || v == nullptr || out == nullptr) return kErrNullPointer;
+  if (head_dim != kHeadDim || batch <= 0 || batch > kMaxCrossBatch || heads <= 0 ||
+      heads > 65535 || q_len <= 0 || kv_len <= 0)
+    return kErrBadShape;
+  if (kv_valid != nullptr) {
+    for (int b = 0; b < batch; ++b)
+      if (kv_valid[b] <= 0 || kv_valid[b] > kv_len) return kErrBadShape;
+  }
+  // Queries through the common checks (their own tiling); keys get their own maps.
+  Launch L;
+  if (int rc = prepare(q, q, q, q_token_stride, q_head_stride, q_batch_stride, 0, q_token_stride,
+                       q_head_stride, q_batch_stride, 0, q_token_stride, q_head_stride,
+                       q_batch_stride, 0, batch, heads, q_len, 1, nullptr, head_dim,
+                       softmax_scale, out, o_token_stride, o_head_stride, o_batch_stride, 0,
+                       status, &L))
+    return rc;
+  if (!aligned16(k) || !aligned16(v) ||
+      !strides_ok(k_token_stride, k_head_stride, k_batch_stride, 0) ||
+      !strides_ok(v_token_stride, v_head_stride, v_batch_stride, 0))
+    return kErrMisaligned;
+  if (make_operand_map(&L.tk, k, kv_len, heads, batch, 1, k_token_stride, k_head_stride,
+                       k_batch_stride, 0) ||
+      make_operand_map(&L.tv, v, kv_len, heads, batch, 1, v_token_stride, v_head_stride,
+                       v_batch_stride, 0))
+    return kErrTensorMap;
+  L.p.kv_tiles_per_seg = (kv_len + kBlockN - 1) / kBlockN;
+  L.p.kv_tiles = L.p.kv_tiles_per_seg;
+  L.p.kv_per_batch = 1;
+  for (int b = 0; b < kMaxCrossBatch; ++b)
+    L.p.kv_valid[b] = b < batch ? (kv_valid != nullptr ? kv_valid[b] : kv_len) : 0;
+  return launch<false>(L, static_cast<unsigned>((L.p.q_tiles + 1) / 2), heads, batch, stream);
 }

@@ -109,7 +109,7 @@ __device__ __forceinline__ void rope8(float (&z)[8], const float (&cs)[8], const
   }
 }
 
-template <int kRopeMode>
+template <int kRopeMode, bool kHasK>
 __global__ void __launch_bounds__(kTokensPerBlock * 32, 3)
     qk_norm_rope_kernel(const PrologueParams p) {
   const int lane = threadIdx.x & 31;
@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(kTokensPerBlock * 32, 3)
   for (int it = 0; it < kChunksPerLane; ++it) {
     const int c0 = it * 256 + lane * 8;
     qv[it] = *reinterpret_cast<const uint4*>(qrow + c0);
-    kv[it] = *reinterpret_cast<const uint4*>(krow + c0);
+    if (kHasK) kv[it] = *reinterpret_cast<const uint4*>(krow + c0);
   }
 
   // fp32 sum of squares over the full 2048-wide rows (squares of BF16 values
@@ -158,9 +158,11 @@ __global__ void __launch_bounds__(kTokensPerBlock * 32, 3)
     unpack8(qv[it], f);
 #pragma unroll
     for (int e = 0; e < 8; ++e) sq4[e & 3] = __fmaf_rn(f[e], f[e], sq4[e & 3]);
-    unpack8(kv[it], f);
+    if (kHasK) {
+      unpack8(kv[it], f);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sk4[e & 3] = __fmaf_rn(f[e], f[e], sk4[e & 3]);
+      for (int e = 0; e < 8; ++e) sk4[e & 3] = __fmaf_rn(f[e], f[e], sk4[e & 3]);
+    }
   }
   float sq = (sq4[0] + sq4[1]) + (sq4[2] + sq4[3]);
   float sk = (sk4[0] + sk4[1]) + (sk4[2] + sk4[3]);
@@ -189,9 +191,11 @@ __global__ void __launch_bounds__(kTokensPerBlock * 32, 3)
     const int c0 = it * 256 + lane * 8;
     float q[8], k[8];
     unpack8(qv[it], q);
-    unpack8(kv[it], k);
     norm8(q, rq, p.wq, c0);
-    norm8(k, rk, p.wk, c0);
+    if (kHasK) {
+      unpack8(kv[it], k);
+      norm8(k, rk, p.wk, c0);
+    }
     if (kRopeMode != 0) {
       float cs[8], sn[8];
       if (kRopeMode == 1) {
@@ -249,10 +253,10 @@ __global__ void __launch_bounds__(kTokensPerBlock * 32, 3)
     if (p.peer) {
       __nv_bfloat16* base = p.dest_base[dest];
       *reinterpret_cast<uint4*>(base + off) = pack8(q);
-      *reinterpret_cast<uint4*>(base + p.k_rel + off) = pack8(k);
+      if (kHasK) *reinterpret_cast<uint4*>(base + p.k_rel + off) = pack8(k);
     } else {
       *reinterpret_cast<uint4*>(p.q_out + dest * p.out_ds + off) = pack8(q);
-      *reinterpret_cast<uint4*>(p.k_out + dest * p.out_ds + off) = pack8(k);
+      if (kHasK) *reinterpret_cast<uint4*>(p.k_out + dest * p.out_ds + off) = pack8(k);
     }
   }
 }
@@ -321,8 +325,11 @@ int qk_norm_rope_impl(const void* q_in, const void* k_in, const void* v_in,
                       void* v_out, int64_t out_token_stride, int64_t out_batch_stride,
                       int64_t out_head_stride, int heads_per_dest, int64_t out_dest_stride,
                       const PeerOut* peer, void* stream) {
-  if (q_in == nullptr || k_in == nullptr || q_out == nullptr || k_out == nullptr)
+  // Q alone (k_in and k_out NULL): the cross-attention query norm, no RoPE, no V.
+  const bool q_only = k_in == nullptr && k_out == nullptr;
+  if (q_in == nullptr || q_out == nullptr || (!q_only && (k_in == nullptr || k_out == nullptr)))
     return kErrNullPointer;
+  if (q_only && (rope_mode != 0 || v_in != nullptr || peer != nullptr)) return kErrBadShape;
   if (hidden != kHidden || batch < 0 || tokens < 0 || heads_per_dest <= 0 ||
       (kHidden / kHeadDimP) % heads_per_dest != 0)
     return kErrBadShape;
@@ -399,10 +406,14 @@ int qk_norm_rope_impl(const void* q_in, const void* k_in, const void* v_in,
   const long long rows = static_cast<long long>(batch) * tokens;
   const unsigned grid = static_cast<unsigned>((rows + kTokensPerBlock - 1) / kTokensPerBlock);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (q_only) {
+    qk_norm_rope_kernel<0, false><<<grid, kTokensPerBlock * 32, 0, s>>>(p);
+    return static_cast<int>(cudaGetLastError());
+  }
   switch (rope_mode) {
-    case 0: qk_norm_rope_kernel<0><<<grid, kTokensPerBlock * 32, 0, s>>>(p); break;
-    case 1: qk_norm_rope_kernel<1><<<grid, kTokensPerBlock * 32, 0, s>>>(p); break;
-    default: qk_norm_rope_kernel<2><<<grid, kTokensPerBlock * 32, 0, s>>>(p); break;
+    case 0: qk_norm_rope_kernel<0, true><<<grid, kTokensPerBlock * 32, 0, s>>>(p); break;
+    case 1: qk_norm_rope_kernel<1, true><<<grid, kTokensPerBlock * 32, 0, s>>>(p); break;
+    default: qk_norm_rope_kernel<2, true><<<grid, kTokensPerBlock * 32, 0, s>>>(p); break;
   }
   return static_cast<int>(cudaGetLastError());
 }

@@ -75,6 +75,9 @@ int erd_rope_axis_table(const float* freqs, int nfreq, int frames, int height, i
  *   out + b*out_batch_stride + t*out_token_stride
  *       + (h % heads_per_dest)*out_head_stride + (h / heads_per_dest)*out_dest_stride + d.
  * Outputs may alias the inputs exactly (in place).
+ * With k_in and k_out NULL (rope_mode 0, no V) only Q is normalised: the
+ * cross-attention query norm (apply_fused_cross_q_rmsnorm,
+ * layers/operator_fusion/cross_q_rmsnorm.py:33-49).
  */
 int erd_qk_norm_rope(const void* q_in, const void* k_in, const void* v_in,
                      int64_t in_token_stride, int64_t in_batch_stride, int batch, int tokens,
@@ -114,6 +117,24 @@ int erd_attn_fwd_bf16(const void* q, const void* k, const void* v, int64_t q_tok
                       float softmax_scale, void* out,
                       int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride,
                       int64_t o_seg_stride, int* status, void* stream);
+
+/*
+ * Cross-attention, head_dim 64: q_len query tokens against kv_len key/value
+ * tokens per (batch, head), BF16 in/out.  kv_valid (host array of `batch`
+ * entries, batch <= 16, or NULL for all kv_len) is the attended prefix of the
+ * keys of each batch entry: the text padding mask of
+ * EraserDiTAttentionProcessor.cross_attn (eraserdit_attention.py:292-332),
+ * whose additive -10000 bias (eraserdit_transformer.py:484-487) drives the
+ * padded keys' weights to exactly zero in fp32.  Strides as erd_attn_fwd_bf16
+ * (one segment).
+ */
+int erd_attn_fwd_cross_bf16(
+    const void* q, const void* k, const void* v, int64_t q_token_stride, int64_t q_head_stride,
+    int64_t q_batch_stride, int64_t k_token_stride, int64_t k_head_stride, int64_t k_batch_stride,
+    int64_t v_token_stride, int64_t v_head_stride, int64_t v_batch_stride, int batch, int heads,
+    int q_len, int kv_len, const int32_t* kv_valid, int head_dim, float softmax_scale, void* out,
+    int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride, int* status,
+    void* stream);
 
 /*
  * Block-sparse variant of erd_attn_fwd_bf16 for the mask-aware pattern.

@@ -201,6 +201,23 @@ def self_attention_layer(
     return out
 
 
+def cross_attention_layer(x: torch.Tensor, enc: torch.Tensor, p: LayerParams,
+                          bias: torch.Tensor | None = None, heads: int = HEADS) -> torch.Tensor:
+    """``EraserDiTAttentionProcessor.cross_attn`` (``eraserdit_attention.py:292-332``):
+    Q from ``x``, K/V from the text ``enc``, RMSNorm across heads on Q and K, no
+    RoPE, SDPA with the additive text bias [B, 1, L] (``prepare_attention_mask``
+    repeats it per head; ``:301-306``), ``to_out[0]``."""
+    batch = x.shape[0]
+    q = rms_norm(F.linear(x, p.wq, p.bq), p.norm_q, p.eps)
+    k = rms_norm(F.linear(enc, p.wk, p.bk), p.norm_k, p.eps)
+    v = F.linear(enc, p.wv, p.bv)
+    qh, kh, vh = (t.unflatten(2, (heads, -1)).transpose(1, 2) for t in (q, k, v))
+    mask = None if bias is None else bias.reshape(batch, 1, 1, -1).to(q.dtype)
+    out = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=mask, dropout_p=0.0,
+                                         is_causal=False)
+    return F.linear(out.transpose(1, 2).flatten(2).to(q.dtype), p.wo, p.bo)
+
+
 def layer_flops(batch: int, seq: int, hidden: int = HIDDEN, heads: int = HEADS,
                 head_dim: int = HEAD_DIM) -> float:
     """Algorithmic FLOPs of one layer: 4 Linear GEMMs + the attention core."""
