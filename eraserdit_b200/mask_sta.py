@@ -46,10 +46,13 @@ class SparsePlan:
                  seg_blocks: list[int] | None = None, tiles_per_seg: int | None = None,
                  order: torch.Tensor | None = None) -> None:
         device = torch.device(device)
-        host = build_schedule(blocks, kv_block, seg_blocks=seg_blocks, tiles_per_seg=tiles_per_seg)
-        self.host: SparseSchedule = host
-        self.schedule = host.schedule.to(device).contiguous()
-        self.entries = host.entries.to(device).contiguous()
+        # The work lists are built where the pattern lives (on the device when
+        # the mask is there: a handful of launches per window, no host loop).
+        built = build_schedule(blocks.to(device), kv_block, seg_blocks=seg_blocks,
+                               tiles_per_seg=tiles_per_seg)
+        self.host: SparseSchedule = built
+        self.schedule = built.schedule.to(device).contiguous()
+        self.entries = built.entries.to(device).contiguous()
         self.blocks = blocks.cpu()
         self.kv_block = kv_block
         self.seg_blocks = seg_blocks
@@ -59,8 +62,11 @@ class SparsePlan:
 
     @classmethod
     def from_mask(cls, mask: torch.Tensor | None, geom: StaGeometry, device, **kw) -> "SparsePlan":
-        order, _ = tile_order(geom)
-        return cls(block_mask(mask, geom), geom.kv_block, device, order=order, **kw)
+        """Pattern and work lists of one window, computed on ``device``."""
+        device = torch.device(device)
+        order, _ = tile_order(geom, device)
+        blocks = block_mask(None if mask is None else mask.to(device), geom, device)
+        return cls(blocks, geom.kv_block, device, order=order, **kw)
 
     def for_segments(self, seg_blocks: list[int], tiles_per_seg: int) -> "SparsePlan":
         """The same pattern over a segmented layout (one segment per source rank)."""

@@ -88,23 +88,23 @@ def _morton(row: torch.Tensor, col: torch.Tensor, bits: int) -> torch.Tensor:
     return code
 
 
-def tile_order(geom: StaGeometry) -> tuple[torch.Tensor, torch.Tensor]:
+def tile_order(geom: StaGeometry, device=None) -> tuple[torch.Tensor, torch.Tensor]:
     """(order, tile_coords): ``order[i]`` is the raster index f*H*W + h*W + w of
     the token at position i of the tile layout; ``tile_coords`` [tiles, 3] the
     (frame, row, column) tile coordinates in layout order."""
     geom.validate()
     tf, th, tw = geom.tile_grid
-    rows = torch.arange(th).repeat_interleave(tw)
-    cols = torch.arange(tw).repeat(th)
+    rows = torch.arange(th, device=device).repeat_interleave(tw)
+    cols = torch.arange(tw, device=device).repeat(th)
     bits = max(1, math.ceil(math.log2(max(th, tw))))
     spatial = torch.argsort(_morton(rows, cols, bits), stable=True)
     rows, cols = rows[spatial], cols[spatial]
-    frames = torch.arange(tf).repeat_interleave(th * tw)
+    frames = torch.arange(tf, device=device).repeat_interleave(th * tw)
     coords = torch.stack([frames, rows.repeat(tf), cols.repeat(tf)], dim=1)  # [tiles, 3]
     t0, t1, t2 = geom.tile
-    df = torch.arange(t0).repeat_interleave(t1 * t2)
-    dh = torch.arange(t1).repeat_interleave(t2).repeat(t0)
-    dw = torch.arange(t2).repeat(t0 * t1)
+    df = torch.arange(t0, device=device).repeat_interleave(t1 * t2)
+    dh = torch.arange(t1, device=device).repeat_interleave(t2).repeat(t0)
+    dw = torch.arange(t2, device=device).repeat(t0 * t1)
     _, gh, gw = geom.grid
     f = coords[:, 0:1] * t0 + df
     h = coords[:, 1:2] * t1 + dh
@@ -123,12 +123,12 @@ def background_blocks(geom: StaGeometry, coords: torch.Tensor | None = None) -> 
     nq = geom.tokens // geom.query_block
     nkv = geom.tokens // geom.kv_block
     centre = torch.div(coords.view(nq, per_q, 3).sum(1), per_q, rounding_mode="floor")
-    extent = torch.tensor(geom.window)
-    limit = torch.tensor(geom.tile_grid) - extent
+    extent = torch.tensor(geom.window, device=coords.device)
+    limit = torch.tensor(geom.tile_grid, device=coords.device) - extent
     start = torch.minimum((centre - extent // 2).clamp_min(0), limit)
     inside = ((coords[None] >= start[:, None]) & (coords[None] < (start + extent)[:, None])).all(-1)
     blocks = inside.view(nq, nkv, per_kv).any(-1)
-    q = torch.arange(nq)
+    q = torch.arange(nq, device=coords.device)
     ratio = geom.query_block // geom.kv_block
     for r in range(max(ratio, 1)):
         blocks[q, q * ratio + r] = True
@@ -142,15 +142,18 @@ def protected_query_blocks(mask: torch.Tensor, order: torch.Tensor, geom: StaGeo
     m = (mask.reshape(geom.grid) > 0).float()[None, None]
     pad = tuple(k // 2 for k in geom.protect)
     dilated = F.max_pool3d(m, geom.protect, stride=1, padding=pad) > 0
-    return dilated.flatten()[order.to(dilated.device)].view(-1, geom.query_block).any(1).cpu()
+    return dilated.flatten()[order.to(dilated.device)].view(-1, geom.query_block).any(1).to(order.device)
 
 
-def block_mask(mask: torch.Tensor | None, geom: StaGeometry) -> torch.Tensor:
-    """The full pattern: background blocks, with protected query rows dense."""
-    order, coords = tile_order(geom)
+def block_mask(mask: torch.Tensor | None, geom: StaGeometry, device=None) -> torch.Tensor:
+    """The full pattern: background blocks, with protected query rows dense
+    (computed on ``device``, the mask's by default)."""
+    if device is None:
+        device = mask.device if mask is not None else torch.device("cpu")
+    order, coords = tile_order(geom, device)
     blocks = background_blocks(geom, coords)
     if mask is not None:
-        blocks[protected_query_blocks(mask, order, geom)] = True
+        blocks[protected_query_blocks(mask.to(device), order, geom)] = True
     return blocks
 
 
@@ -243,46 +246,49 @@ def build_schedule(blocks: torch.Tensor, kv_block: int, seg_blocks: list[int] | 
     """Pair the 128-row query tiles and list each pair's key tiles.
 
     ``blocks`` is a bool [query blocks of 128, key blocks of ``kv_block``] mask
-    over the tile-ordered sequence.  With ``seg_blocks`` the sequence is held
-    as segments (one per source rank of the sequence-parallel exchange) of that
-    many 128-token blocks each, in slots of ``tiles_per_seg`` tiles; tile
-    indices are then those of the segmented layout.
+    over the tile-ordered sequence, on any device (the lists are built there,
+    without host loops).  With ``seg_blocks`` the sequence is held as segments
+    (one per source rank of the sequence-parallel exchange) of that many
+    128-token blocks each, in slots of ``tiles_per_seg`` tiles; tile indices
+    are then those of the segmented layout.
+
+    Full rows are paired with full rows, the others with their neighbours in
+    tile order; rows with the longest lists come first (the hardware
+    dispatches CTAs in grid order).
     """
-    blocks = blocks.cpu()
+    device = blocks.device
     halves = _halves(blocks, kv_block)  # [nq, nt]
     nq, nt = halves.shape
     if nq != nt:
         raise ValueError("self-attention: as many key tiles as query tiles")
     tps = tiles_per_seg if tiles_per_seg is not None else nq
-    tile_of = block_tiles(nq, seg_blocks, tps)
+    tile_of = block_tiles(nq, seg_blocks, tps).to(device)
     counts = (halves != 0).sum(1)
     if bool((counts == 0).any()):
         raise ValueError("every query block needs at least one key block")
     full = counts == nt
-    order = torch.cat([torch.nonzero(full).flatten(), torch.nonzero(~full).flatten()]).tolist()
-    pairs = [(order[i], order[i + 1] if i + 1 < len(order) else -1)
-             for i in range(0, len(order), 2)]
-    rows, entries = [], []
-    issued = 0
-    for a, b in pairs:
-        ha = halves[a]
-        hb = halves[b] if b >= 0 else torch.zeros_like(ha)
-        cols = torch.nonzero((ha | hb) != 0).flatten()
-        code = tile_of[cols] | (ha[cols] << 24) | (hb[cols] << 26)
-        rows.append((len(cols), int(tile_of[a]), int(tile_of[b]) if b >= 0 else -1, code))
-        issued += len(cols) * KV_TILE * QUERY_TILE * (2 if b >= 0 else 1)
-    # Longest lists first: the hardware dispatches CTAs in grid order.
-    rows.sort(key=lambda r: -r[0])
-    sched = torch.empty(len(rows), 4, dtype=torch.int64)
-    first = 0
-    for i, (n, qa, qb, code) in enumerate(rows):
-        sched[i] = torch.tensor([qa, qb, first, n])
-        entries.append(code)
-        first += n
-    ent = torch.cat(entries)
-    bits_per_half = 64
-    kept = int(sum(((halves >> s) & 1).sum() for s in range(2))) * bits_per_half * QUERY_TILE
-    return SparseSchedule(sched.to(torch.int32), ent.to(torch.int32), kept, issued,
+    idx = torch.arange(nq, device=device)
+    order = torch.cat([idx[full], idx[~full]])
+    npairs = (nq + 1) // 2
+    slots = torch.full((2 * npairs,), -1, dtype=torch.int64, device=device)
+    slots[:nq] = order
+    pa, pb = slots[0::2], slots[1::2]  # pb is -1 for a lone last tile
+    ha = halves[pa]
+    hb = torch.where((pb >= 0)[:, None], halves[pb.clamp_min(0)], torch.zeros_like(ha))
+    union = (ha | hb) != 0
+    n = union.sum(1)
+    rank = torch.argsort(-n, stable=True)
+    union, ha, hb, pa, pb, n = union[rank], ha[rank], hb[rank], pa[rank], pb[rank], n[rank]
+    row, col = torch.nonzero(union, as_tuple=True)  # grouped by row, columns ascending
+    entries = tile_of[col] | (ha[row, col] << 24) | (hb[row, col] << 26)
+    first = torch.cumsum(n, 0) - n
+    qb = torch.where(pb >= 0, tile_of[pb.clamp_min(0)], torch.full_like(pb, -1))
+    sched = torch.stack([tile_of[pa], qb, first, n], dim=1)
+    # every CTA computes both of its tiles' products (a lone tile's partner
+    # repeats it), so the issued work counts two tiles per list entry
+    issued = int(n.sum()) * KV_TILE * QUERY_TILE * 2
+    kept = int(((halves & 1) + ((halves >> 1) & 1)).sum()) * 64 * QUERY_TILE
+    return SparseSchedule(sched.to(torch.int32), entries.to(torch.int32), kept, issued,
                           nq * QUERY_TILE * nt * KV_TILE)
 
 
