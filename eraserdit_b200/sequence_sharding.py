@@ -109,3 +109,53 @@ def plan_sequence_shards(global_length: int, sp_degree: int,
         plans.append(SequenceShardPlan(global_length, padded, start, start + local, valid,
                                        local - valid, owner_rank, sp_degree, rank))
     return tuple(plans)
+
+
+# Attention backends that may run under sequence parallelism (the reference's
+# set, sequence_parallel.py:88-99, plus the two B200 backends).
+SP_BACKENDS = frozenset({"torch_sdpa", "flash_attn", "sage_attn", "sage_fp8", "b200_native",
+                         "b200_fp8"})
+
+
+@dataclass(frozen=True)
+class SequenceParallelMetadata:
+    """One SP rank's shard and backend contract (``layers/attention/sequence_parallel.py:57-154``).
+
+    The fields and checks are those of a :class:`SequenceShardPlan` plus the
+    attention backend, which must be one that runs under sequence parallelism.
+    """
+
+    global_length: int
+    padded_length: int
+    local_start: int
+    local_end: int
+    valid_local_length: int
+    pad_right: int
+    owner_rank: int
+    sp_degree: int
+    rank: int
+    backend: object  # an AttentionBackendEnum member
+
+    def __post_init__(self) -> None:
+        # The shard fields obey exactly the plan's contract.
+        SequenceShardPlan(self.global_length, self.padded_length, self.local_start,
+                          self.local_end, self.valid_local_length, self.pad_right,
+                          self.owner_rank, self.sp_degree, self.rank)
+        from .attention import AttentionBackendEnum
+        if not isinstance(self.backend, AttentionBackendEnum):
+            raise TypeError("backend must be an AttentionBackendEnum")
+        if self.backend.value not in SP_BACKENDS:
+            raise ValueError("backend must be one of " + ", ".join(sorted(SP_BACKENDS))
+                             + " for sequence parallel")
+
+    @property
+    def local_length(self) -> int:
+        return self.local_end - self.local_start
+
+    @classmethod
+    def from_shard_plan(cls, plan: SequenceShardPlan, *, backend) -> "SequenceParallelMetadata":
+        if not isinstance(plan, SequenceShardPlan):
+            raise TypeError("plan must be a SequenceShardPlan")
+        return cls(plan.global_length, plan.padded_length, plan.local_start, plan.local_end,
+                   plan.valid_local_length, plan.pad_right, plan.owner_rank, plan.sp_degree,
+                   plan.rank, backend)

@@ -112,3 +112,35 @@ class DiTGroups:
 
     def get(self, axis: str):
         return self.groups[axis]
+
+
+def cfg_branches(topology: DiTTopology, cfg_rank: int) -> tuple[str, ...]:
+    """The guidance branches this rank computes (``nccl_runner.py:92``): both on
+    one CFG group, otherwise the positive branch on CFG rank 0 and the negative
+    one on rank 1."""
+    if topology.cfg == 1:
+        return ("positive", "negative")
+    return ("positive",) if cfg_rank == 0 else ("negative",)
+
+
+def gather_cfg_pair(local: torch.Tensor, groups: DiTGroups, owner_only: bool = False):
+    """Assemble the two CFG branches' outputs (``nccl_runner.py:127-137``).
+
+    Returns ``(negative, positive)`` on every rank of the CFG group, or only on
+    its first rank with ``owner_only`` (the others get ``None``).  With one CFG
+    group there is nothing to gather: ``local`` must then be a mapping
+    ``{"positive": ..., "negative": ...}``.
+    """
+    if groups.topology.cfg == 1:
+        return local["negative"], local["positive"]
+    group, ranks, _ = groups.get("cfg")
+    local = local.contiguous()
+    if owner_only:
+        pair = [torch.empty_like(local) for _ in ranks] if groups.rank == ranks[0] else None
+        dist.gather(local, gather_list=pair, dst=ranks[0], group=group)
+        if pair is None:
+            return None
+    else:
+        pair = [torch.empty_like(local) for _ in ranks]
+        dist.all_gather(pair, local, group=group)
+    return pair[1], pair[0]

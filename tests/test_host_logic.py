@@ -49,3 +49,25 @@ def test_block_partition():
     assert all((e - s) % 128 == 0 for s, e in bounds)
     with pytest.raises(ValueError):
         block_bounds(1000, 2, 0)
+
+
+def test_sequence_parallel_metadata():
+    from eraserdit_b200.attention import AttentionBackendEnum
+    from eraserdit_b200.sequence_sharding import SequenceParallelMetadata
+    plans = plan_sequence_shards(10, 4, 0)
+    meta = SequenceParallelMetadata.from_shard_plan(plans[3], backend=AttentionBackendEnum.B200_NATIVE)
+    assert (meta.local_start, meta.local_end, meta.valid_local_length, meta.pad_right) == (9, 12, 1, 2)
+    assert meta.local_length == 3
+    with pytest.raises(TypeError):
+        SequenceParallelMetadata.from_shard_plan(plans[0], backend="b200_native")
+    with pytest.raises(ValueError):  # the plan's own contract
+        SequenceParallelMetadata(10, 12, 3, 6, 2, 1, 0, 4, 1, AttentionBackendEnum.TORCH_SDPA)
+    with pytest.raises(TypeError):
+        SequenceParallelMetadata.from_shard_plan(object(), backend=AttentionBackendEnum.SAGE_FP8)
+
+
+def test_cfg_branches():
+    from eraserdit_b200.topology import cfg_branches
+    assert cfg_branches(DiTTopology(ulysses=8), 0) == ("positive", "negative")
+    assert cfg_branches(DiTTopology(ulysses=4, cfg=2), 0) == ("positive",)
+    assert cfg_branches(DiTTopology(ulysses=4, cfg=2), 1) == ("negative",)

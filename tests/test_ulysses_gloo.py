@@ -115,3 +115,33 @@ def test_two_rank_exchange_and_peer_failure():
         r1 = open(os.path.join(d, "r1")).read().split("|")
     assert r0 == ["ok", "ok", "peer (1,)", "ok"]
     assert r1 == ["ok", "ok", "injected attention failure", "ok"]
+
+
+
+def _cfg_rank(rank, world, port, result_dir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        from eraserdit_b200.topology import DiTGroups, DiTTopology, cfg_branches, gather_cfg_pair
+        groups = DiTGroups(DiTTopology(cfg=2), warm_up=False)
+        branch = cfg_branches(groups.topology, groups.coordinates[3])[0]
+        local = torch.full((2, 3), 1.0 if branch == "positive" else -1.0) * (rank + 1)
+        negative, positive = gather_cfg_pair(local, groups)
+        owner = gather_cfg_pair(local, groups, owner_only=True)
+        ok = (float(negative[0, 0]) == -2.0 and float(positive[0, 0]) == 1.0
+              and ((owner is None) == (rank != 0)))
+        with open(os.path.join(result_dir, f"c{rank}"), "w") as f:
+            f.write(f"{branch}|{ok}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_cfg_pair_gather_two_ranks():
+    """CFG2: rank 0 computes the positive branch, rank 1 the negative one; the
+    pair gather returns (negative, positive) (nccl_runner.py:92,127-137)."""
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_cfg_rank, args=(2, _free_port(), d), nprocs=2, join=True,
+                           start_method="spawn")
+        got = [open(os.path.join(d, f"c{r}")).read() for r in range(2)]
+    assert got == ["positive|True", "negative|True"]
