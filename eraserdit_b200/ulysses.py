@@ -54,6 +54,7 @@ the received segments.
 
 from __future__ import annotations
 
+from contextlib import nullcontext
 from dataclasses import dataclass
 from typing import Callable
 
@@ -171,8 +172,16 @@ class UlyssesSelfAttention:
     def partition(self, length: int) -> slice:
         if length < self.degree:
             raise ValueError("sequence length must be at least SP degree")
+        self.length = length  # the reference hook's contract: attention() follows partition()
         start, end = self._bounds(length, self.rank)
         return slice(start, end)
+
+    def linear_scope(self, model, mode):
+        """The reference's hook (``mesh.py:172-270``) pads the projections' GEMM
+        rows to keep BF16 results identical across SP degrees; here projections
+        run on the local rows only, so the scope changes nothing."""
+        del model, mode
+        return nullcontext()
 
     def chunks_for(self, length: int) -> int:
         if self.head_chunks is not None:
@@ -289,8 +298,8 @@ class UlyssesSelfAttention:
                   for d in range(self.degree)]
         return outputs, inputs
 
-    def post(self, step: _Step) -> torch.Tensor:
-        """Peer error check, head gather, output projection."""
+    def gather_heads(self, step: _Step) -> torch.Tensor:
+        """Peer error check and the heads of this rank's tokens, [B, L_rank, 2048]."""
         flags = step.recv2[:, :, 0].float().amax(dim=0)
         if step.failed:
             raise RuntimeError("local sequence-parallel attention failed")
@@ -302,8 +311,53 @@ class UlyssesSelfAttention:
         hc = self.local_heads // c
         # head = source rank * Hl + chunk * Hc + head within the chunk
         heads = step.recv2[:, :, FLAG:].view(c, n, lme, b, hc, HEAD_DIM)
-        attn = heads.permute(3, 2, 1, 0, 4, 5).reshape(b, lme, n * c * hc * HEAD_DIM)
-        return self.layer.project_out(attn)
+        return heads.permute(3, 2, 1, 0, 4, 5).reshape(b, lme, n * c * hc * HEAD_DIM)
+
+    def post(self, step: _Step) -> torch.Tensor:
+        """Peer error check, head gather, output projection."""
+        return self.layer.project_out(self.gather_heads(step))
+
+    # ------------------------------------------- attention-level SP hook
+    def attention_pre(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                      length: int) -> _Step:
+        """Pack this rank's normalised, rotated [B, L_rank, H, 64] Q/K/V into the
+        send buffer (the reference's ``pack_qkv``, ``qkv_packing.py:31-48``)."""
+        batch, lme, heads, dim = query.shape
+        if heads != self.layer.heads or dim != HEAD_DIM:
+            raise ValueError("query must be [B, L_rank, heads, 64]")
+        lengths, send1, recv1, send2, recv2, _, _ = self._buffers_for(
+            batch, length, query.device, query.dtype, 1)
+        if lme != lengths[self.rank]:
+            raise ValueError("local sequence length must match the rank's partition")
+        n, hl = self.degree, self.local_heads
+        for i, x in enumerate((query, key, value)):
+            # send1[dest][0][token][qkv][b][head][d] <- x[b][token][dest * hl + head][d]
+            send1[:, 0, :, i] = x.view(batch, lme, n, hl, dim).permute(2, 1, 0, 3, 4)
+        start, _ = self._bounds(length, self.rank)
+        return _Step(batch, length, lengths, start, send1, recv1, send2, recv2)
+
+    def attention(self, query, key, value, impl=None, metadata=None) -> torch.Tensor:
+        """The reference's SP hook (``nccl_sequence.py:235-260``): attention of
+        this rank's [B, L_rank, H, 64] queries over the whole sequence; returns
+        [B, L_rank, H, 64].  ``partition(length)`` must have been called."""
+        if impl is not None and (getattr(impl, "causal", False) or getattr(impl, "dropout", 0)):
+            raise ValueError("distributed DiT self-attention requires noncausal SDPA, dropout 0")
+        if metadata is not None and getattr(metadata, "attn_mask", None) is not None:
+            raise ValueError("distributed DiT self-attention requires an unmasked SDPA")
+        length = getattr(self, "length", None)
+        if length is None:
+            raise RuntimeError("call partition(length) before attention()")
+        step = self.attention_pre(query, key, value, length)
+        self.exchange(*self.send_recv_1(step))
+        error = None
+        try:
+            self.attend(step)
+        except Exception as exc:  # every rank still enters the second exchange
+            error = exc
+        self.exchange(*self.send_recv_2(step))
+        if error is not None:
+            raise error
+        return self.gather_heads(step).view(query.shape)
 
     # ----------------------------------------------------- peer transport
     def peer_buffers(self, batch: int, length: int, device, connect=True):
@@ -527,6 +581,32 @@ def select_head_chunks(degree: int, length: int, local_heads: int, *, sparse: bo
     """
     del degree, length, local_heads, sparse
     return 1
+
+
+def emulate_attention_hook(layer: EraserDiTSelfAttention, degree: int, q: torch.Tensor,
+                           k: torch.Tensor, v: torch.Tensor) -> list[torch.Tensor]:
+    """All ranks of the attention-level hook in one process (chunks exchanged
+    by copies); q/k/v are the full [B, S, H, 64] tensors, each rank gets its
+    slice.  Returns every rank's [B, L_rank, H, 64] output."""
+    length = q.shape[1]
+    ranks = [UlyssesSelfAttention(layer, degree, r, exchange=None) for r in range(degree)]
+    steps = []
+    for r in ranks:
+        sl = r.partition(length)
+        steps.append(r.attention_pre(q[:, sl].contiguous(), k[:, sl].contiguous(),
+                                     v[:, sl].contiguous(), length))
+
+    def all_to_all(pairs):
+        for dst in range(degree):
+            outputs, _ = pairs[dst]
+            for src in range(degree):
+                outputs[src].copy_(pairs[src][1][dst])
+
+    all_to_all([r.send_recv_1(s) for r, s in zip(ranks, steps)])
+    for r, s in zip(ranks, steps):
+        r.attend(s)
+    all_to_all([r.send_recv_2(s) for r, s in zip(ranks, steps)])
+    return [r.gather_heads(s).view(q.shape[0], -1, q.shape[2], 64) for r, s in zip(ranks, steps)]
 
 
 def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, rope,

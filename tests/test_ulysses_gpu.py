@@ -126,3 +126,20 @@ def test_peer_transport_fp8_and_sparse(degree, kind):
     peer = emulate_ranks(layer, degree, x, rope, sparse=plan, transport="peer")
     for a, b in zip(nccl, peer):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("degree", [2, 8])
+def test_attention_level_hook(degree):
+    """The reference's SP hook contract (partition, then attention(q, k, v, impl,
+    metadata) on the local [B, L_rank, H, 64] tensors): equal to single-GPU
+    attention over the whole sequence."""
+    from eraserdit_b200.attention import attention_bshd
+    from eraserdit_b200.ulysses import emulate_attention_hook
+    layer, _, _ = _setup(2, 8, 12, 1, seed=30 + degree)
+    g = torch.Generator(device="cuda").manual_seed(31)
+    q, k, v = [torch.randn(2, 190, 32, 64, generator=g, device="cuda").bfloat16() for _ in range(3)]
+    parts = emulate_attention_hook(layer, degree, q, k, v)
+    got = torch.cat(parts, dim=1)
+    want = attention_bshd(q, k, v, 0.125)
+    assert max_abs(got, want) <= 1e-2
+    assert cosine(got, want) >= 0.99999
