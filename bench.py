@@ -452,9 +452,15 @@ def main() -> None:
                         help="Ulysses exchange: peer-memory stores over NVLink or NCCL all-to-all")
     parser.add_argument("--head-chunks", type=int, default=None,
                         help="Ulysses head chunks (exchange/attention overlap); default: policy")
+    parser.add_argument("--ring", type=int, default=1,
+                        help="ring degree of Ulysses x Ring (USP) sequence parallelism")
+    parser.add_argument("--ring-mode", default="streaming", choices=["reference", "streaming"],
+                        help="ring mode: gather every K/V piece, or pieces with a carried state")
     args = parser.parse_args()
     if args.fp8 and args.sparse:
         parser.error("--fp8 and --sparse are separate configurations")
+    if args.ring > 1 and (args.fp8 or args.sparse or args.qkv_fp8):
+        parser.error("the ring path computes dense BF16 attention")
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)

@@ -19,7 +19,7 @@ from pathlib import Path
 import torch
 
 LIBRARY_PATH = Path(__file__).resolve().parent / "liberaserdit_b200.so"
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 _c_int, _c_i64, _c_float, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -56,6 +56,10 @@ SIGNATURES = {
     "erd_quantize_e4m3": [_vp, _vp, _c_i64, _c_float, _vp],
     "erd_attn_fwd_cross_bf16": [_vp, _vp, _vp] + [_c_i64] * 9 + [_c_int] * 4
                                + [_vp, _c_int, _c_float, _vp] + [_c_i64] * 3 + [_vp, _vp],
+    "erd_ring_state_bytes": [_c_int, _c_int, _c_int, _c_int],
+    "erd_attn_fwd_ring_bf16": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 4
+                              + [_vp, _c_int, _c_int, _vp, _c_int, _c_float, _vp] + [_c_i64] * 4
+                              + [_vp, _vp, ctypes.c_size_t, _c_int, _vp, _vp],
     "erd_peer_alloc": [ctypes.c_size_t, ctypes.POINTER(_vp)],
     "erd_peer_free": [_vp],
     "erd_peer_ipc_handle": [_vp, _vp],
@@ -70,7 +74,8 @@ SIGNATURES = {
     "erd_attn_fwd_fp8_static_scratch": [_vp, _vp, _vp] + [_c_i64] * 12 + [_c_int] * 4
                                        + [_vp, _c_int, _c_float, _vp] + [_c_i64] * 4 + [_vp, _vp],
 }
-RESTYPES = {"erd_error_string": ctypes.c_char_p, "erd_attn_fp8_workspace_bytes": ctypes.c_size_t}
+RESTYPES = {"erd_error_string": ctypes.c_char_p, "erd_attn_fp8_workspace_bytes": ctypes.c_size_t,
+            "erd_ring_state_bytes": ctypes.c_size_t}
 
 _lib = None
 _lock = threading.Lock()

@@ -1,9 +1,11 @@
-"""Multi-GPU leg of ``bench.py``: Ulysses SP (optionally CFG x SP) over NCCL.
+"""Multi-GPU leg of ``bench.py``: Ulysses SP (optionally CFG x SP, or
+Ulysses x Ring with ``--ring``) with peer-memory or NCCL exchanges.
 
 Launched by torchrun with one process per GPU.  Every rank builds the same
 seeded layer and input, keeps its floor-partitioned tokens (CFG: its branch's
-batch entry) and runs the Ulysses layer; per-rank times come from CUDA events
-and the reported time is the maximum over ranks (an all-reduce MAX)."""
+batch entry) and runs the sequence-parallel layer; per-rank times come from
+CUDA events and the reported time is the maximum over ranks (an all-reduce
+MAX)."""
 
 from __future__ import annotations
 
@@ -26,6 +28,7 @@ def run_sequence_parallel(args) -> None:
     import bench as B
     from eraserdit_b200 import _native
     from eraserdit_b200.topology import DiTGroups, DiTTopology
+    from eraserdit_b200.ring import UspSelfAttention, ring_rotate
     from eraserdit_b200.ulysses import UlyssesSelfAttention, peer_exchange
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -37,12 +40,13 @@ def run_sequence_parallel(args) -> None:
     torch.cuda.set_device(device)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     try:
-        cfg = args.cfg
-        if world % cfg or B.BATCH % cfg:
-            raise SystemExit("CFG degree must divide the GPU count and the batch")
-        topo = DiTTopology(ulysses=world // cfg, cfg=cfg)
+        cfg, ring = args.cfg, getattr(args, "ring", 1)
+        if world % (cfg * ring) or B.BATCH % cfg:
+            raise SystemExit("CFG x ring degree must divide the GPU count, CFG the batch")
+        topo = DiTTopology(ulysses=world // (cfg * ring), ring=ring, cfg=cfg)
         groups = DiTGroups(topo)
-        group, ranks, index = groups.get("ulysses") if world // cfg > 1 else (None, (rank,), 0)
+        group, ranks, index = (groups.get("ulysses") if topo.ulysses > 1
+                               else (None, (rank,), 0))
         cfg_index = topo.coordinates(rank)[3]
         layer, rope = B.build_problem(device, "fp8" if args.fp8 else "bf16")
         plan, kept, issued = B.build_sparse_plan(device) if args.sparse else (None, 1.0, 1.0)
@@ -50,10 +54,21 @@ def run_sequence_parallel(args) -> None:
         x_full = torch.randn(B.BATCH, B.SEQ, B.HIDDEN, generator=g, device=device).bfloat16()
         per_branch = B.BATCH // cfg
         x_branch = x_full[cfg_index * per_branch:(cfg_index + 1) * per_branch]
-        transport = args.transport
-        sp = UlyssesSelfAttention(layer, len(ranks), index, peer_exchange(group, ranks, index),
-                                  group_ranks=ranks, sparse=plan, head_chunks=args.head_chunks,
-                                  transport=transport, group=group)
+        transport = args.transport if ring == 1 else "nccl"
+
+        def make_layer():
+            if ring > 1:
+                rgroup, rranks, rindex = groups.get("ring")
+                return UspSelfAttention(layer, len(ranks), index,
+                                        peer_exchange(group, ranks, index), ring, rindex,
+                                        ring_rotate(rgroup, rranks, rindex), group_ranks=ranks,
+                                        mode=args.ring_mode)
+            return UlyssesSelfAttention(layer, len(ranks), index,
+                                        peer_exchange(group, ranks, index), group_ranks=ranks,
+                                        sparse=plan, head_chunks=args.head_chunks,
+                                        transport=transport, group=group)
+
+        sp = make_layer()
         x_local = x_branch[:, sp.partition(B.SEQ)].contiguous()
         del x_full
         stream = torch.cuda.current_stream(device)
@@ -90,9 +105,7 @@ def run_sequence_parallel(args) -> None:
         # both in the same order.
         host_x = x_local.cpu().pin_memory()
         host_y = [torch.empty_like(host_x).pin_memory() for _ in range(2)]
-        sp2 = UlyssesSelfAttention(layer, len(ranks), index, peer_exchange(group, ranks, index),
-                                   group_ranks=ranks, sparse=plan, head_chunks=args.head_chunks,
-                                   transport=transport, group=group)
+        sp2 = make_layer()
         objects = [sp, sp2]
         dist.barrier()
         e2e_ms = B.run_e2e(lambda xd, i=[0]: _alternate(objects, i, xd, rope, B.SEQ), host_x,
@@ -119,15 +132,22 @@ def run_sequence_parallel(args) -> None:
             achieved = local_attn_flop / (kernel_ms / 1e3) / 1e12
             layer_flop = B.LINEAR_FLOP + B.ATTN_FLOP * kept
             parallelism = f"cfg{cfg}xsp{world // cfg}" if cfg > 1 else f"sp{world}"
+            if ring > 1:
+                parallelism += f" (ulysses{topo.ulysses} x ring{ring}, {args.ring_mode} ring)"
             parallelism += f", {transport} exchange"
             chunks = sp.chunks_for(B.SEQ)
             if chunks > 1:
                 parallelism += f", {chunks} head chunks"
+            attn_launches = chunks
+            if ring > 1 and args.ring_mode != "reference":
+                attn_launches = ring
             if plan is not None:
                 workload = B.SPARSE_WORKLOAD + ", Ulysses SP (whole 128-token blocks per rank)"
                 kernel = "attn_fwd_bf16 (block-sparse instantiation)"
             else:
-                workload = B.WORKLOAD.replace("config 1", "config 2 (Ulysses SP)")
+                workload = B.WORKLOAD.replace(
+                    "config 1", "config 2 (Ulysses x Ring SP)" if ring > 1
+                    else "config 2 (Ulysses SP)")
                 kernel = "attn_fwd_fp8" if args.fp8 else "attn_fwd_bf16"
             line = {
                 "metric": B.METRIC, "value": layer_flop / (ms / 1e3) / 1e12, "unit": B.UNIT,
@@ -148,7 +168,7 @@ def run_sequence_parallel(args) -> None:
                         "h2d_bytes_per_step": host_x.numel() * host_x.element_size() * world,
                         "d2h_bytes_per_step": host_y[0].numel() * host_y[0].element_size() * world,
                         "streams": 2},
-                "gpu_launches": (1 + (3 if args.fp8 else 1) * chunks) * args.steps,
+                "gpu_launches": (1 + (3 if args.fp8 else 1) * attn_launches) * args.steps,
                 "clocks": clock,
             }
             if plan is not None:

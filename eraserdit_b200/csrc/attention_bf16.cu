@@ -87,7 +87,20 @@ struct AttnParams {
   int kv_tiles, kv_tiles_per_seg;
   int kv_per_batch;
   int kv_valid[kMaxCrossBatch];
+  // Valid tokens of each key / value segment (the query's seg_lens for
+  // self-attention; a ring piece's own lengths otherwise).
+  int kv_seg_lens[kMaxSegments];
+  // Carried softmax state (kState instantiation only): per query tile, O as
+  // 64 x 128 fp32 (column-major: column c of row r at c * 128 + r), then the
+  // running max (log2 domain) and sum of its 128 rows.  state_mode bits:
+  // kStateRead starts from it, kStateWrite stores it instead of the output.
+  float* state;
+  int state_mode;
 };
+
+constexpr int kStateRead = 1;
+constexpr int kStateWrite = 2;
+constexpr int kStateFloatsPerTile = kHeadDim * kBlockM + 2 * kBlockM;
 
 constexpr uint32_t kEntryTileMask = (1u << 24) - 1;
 
@@ -119,11 +132,12 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_per_seg, int& se
   l0 = (tile - seg * tiles_per_seg) * kBlockN;
 }
 
-template <bool kSparse>
+template <bool kSparse, bool kState>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap tmap_q,
                          const __grid_constant__ CUtensorMap tmap_k,
                          const __grid_constant__ CUtensorMap tmap_v, const AttnParams p) {
+  static_assert(!(kSparse && kState), "the carried state serves dense pieces only");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -252,6 +266,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                       (accumulate || k > 0) ? 1u : 0u);
         }
       };
+      // With a carried state O starts from the stored rows (written to TMEM by
+      // the softmax warps before their first P), so every P V accumulates.
+      const bool acc_first = kState && (p.state_mode & kStateRead);
       bool ok = mbar_wait(smem_u32(&bars->q_full), 0, abort, p.status, kStatusTimeoutMma) &&
                 mbar_wait(smem_u32(&bars->k_full[0]), 0, abort, p.status, kStatusTimeoutMma);
       if (ok) {
@@ -280,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           issue_qk(0, s1);
           mma_commit(smem_u32(&bars->s_full[0]));
         }
-        issue_pv(0, s, j > 0);
+        issue_pv(0, s, j > 0 || acc_first);
         mma_commit(smem_u32(&bars->o_done[0]));
         // query tile B
         if (!mbar_wait(smem_u32(&bars->p_full[1]), j & 1, abort, p.status, kStatusTimeoutMma)) break;
@@ -290,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(smem_u32(&bars->s_full[1]));
           mma_commit(smem_u32(&bars->k_empty[s1]));
         }
-        issue_pv(1, s, j > 0);
+        issue_pv(1, s, j > 0 || acc_first);
         mma_commit(smem_u32(&bars->o_done[1]));
         mma_commit(smem_u32(&bars->v_empty[s]));
       }
@@ -310,6 +327,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_run = -CUDART_INF_F;  // running max of S * c (log2 domain)
     float l_run = 0.f;
     bool ok = true;
+    // Carried state of this thread's query row (kState).  The warpgroup of an
+    // odd tile count's missing B tile starts from zeros and never writes.
+    float* st_o = nullptr;
+    const bool state_in = kState && (p.state_mode & kStateRead);
+    if (kState) {
+      const int qt_own = t == 0 ? q_tile_a : q_tile_b;
+      const bool own_valid = qt_own >= 0 && qt_own < p.q_tiles;
+      const long long tile = (static_cast<long long>(batch) * gridDim.y + head) * p.q_tiles +
+                             (own_valid ? qt_own : 0);
+      st_o = p.state + tile * kStateFloatsPerTile;
+      if (state_in) {
+        if (own_valid) {
+          m_run = st_o[kHeadDim * kBlockM + row];
+          l_run = st_o[kHeadDim * kBlockM + kBlockM + row];
+        }
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          uint32_t o[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            o[i] = own_valid ? __float_as_uint(st_o[(h * 32 + i) * kBlockM + row]) : 0u;
+          tmem_st32(tO + h * 32, o);
+        }
+        tmem_wait_st();
+      }
+    }
     for (int j = 0; j < n_kv; ++j) {
       // The list entry is read before the wait, which hides its latency.
       const uint32_t entry = kSparse ? __ldg(list + j) : 0u;
@@ -329,14 +372,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (halves != 0 && kv < p.kv_tiles) {
           int seg, l0;
           tile_coords(kv, p.kv_tiles_per_seg, seg, l0);
-          hi = min(kBlockN, (p.kv_per_batch ? p.kv_valid[batch] : p.seg_lens[seg]) - l0);
+          hi = min(kBlockN, (p.kv_per_batch ? p.kv_valid[batch] : p.kv_seg_lens[seg]) - l0);
           if (!(halves & 2u)) hi = min(hi, kBlockN / 2);
           if (!(halves & 1u)) lo = kBlockN / 2;
         }
       } else {
         int seg, l0;
         tile_coords(j, p.kv_tiles_per_seg, seg, l0);
-        hi = min(kBlockN, (p.kv_per_batch ? p.kv_valid[batch] : p.seg_lens[seg]) - l0);
+        hi = min(kBlockN, (p.kv_per_batch ? p.kv_valid[batch] : p.kv_seg_lens[seg]) - l0);
       }
       // Pass 1: row max over the whole S row (registers released afterwards).
       // A key tile this query tile does not attend at all (sparse lists only)
@@ -363,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool rescale = false;
       if (m_tile > m_run + kRescaleThreshold) {
         m_new = m_tile;
-        rescale = j > 0;
+        rescale = j > 0 || state_in;
       }
       if (j > 0) {
         // P_t and O_t are free once the previous P V product has completed.
@@ -437,7 +480,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld_wait_64(tO, oflat);
       uint32_t(&o)[2][32] = *reinterpret_cast<uint32_t(*)[2][32]>(oflat);
       const int qt = t == 0 ? q_tile_a : q_tile_b;
-      if (qt >= 0 && qt < p.q_tiles) {
+      if (kState && (p.state_mode & kStateWrite)) {
+        if (qt >= 0 && qt < p.q_tiles) {
+          // one fp32 column per store: 128 contiguous bytes per warp
+#pragma unroll
+          for (int i = 0; i < kHeadDim; ++i) st_o[i * kBlockM + row] = __uint_as_float(oflat[i]);
+          st_o[kHeadDim * kBlockM + row] = m_run;
+          st_o[kHeadDim * kBlockM + kBlockM + row] = l_run;
+        }
+      } else if (qt >= 0 && qt < p.q_tiles) {
         int seg, l0;
         tile_coords(qt, p.tiles_per_seg, seg, l0);
         const int tok = l0 + row;
@@ -570,19 +621,28 @@ int prepare(const void* q, const void* k, const void* v, int64_t q_token_stride,
   p.kv_tiles_per_seg = tiles_per_seg;
   p.kv_per_batch = 0;
   for (int b = 0; b < kMaxCrossBatch; ++b) p.kv_valid[b] = 0;
+  for (int s = 0; s < kMaxSegments; ++s) p.kv_seg_lens[s] = p.seg_lens[s];
+  p.state = nullptr;
+  p.state_mode = 0;
   return kErrOk;
 }
 
-template <bool kSparse>
+template <bool kSparse, bool kState = false>
 int launch(const Launch& L, unsigned ctas, int heads, int batch, void* stream) {
-  cudaError_t e = cudaFuncSetAttribute(attn_fwd_bf16_kernel<kSparse>,
+  cudaError_t e = cudaFuncSetAttribute(attn_fwd_bf16_kernel<kSparse, kState>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kSmemLaunchBytes);
   if (e != cudaSuccess) return static_cast<int>(e);
   const dim3 grid(ctas, static_cast<unsigned>(heads), static_cast<unsigned>(batch));
-  attn_fwd_bf16_kernel<kSparse><<<grid, kThreads, kSmemLaunchBytes,
-                                  static_cast<cudaStream_t>(stream)>>>(L.tq, L.tk, L.tv, L.p);
+  attn_fwd_bf16_kernel<kSparse, kState><<<grid, kThreads, kSmemLaunchBytes,
+                                          static_cast<cudaStream_t>(stream)>>>(L.tq, L.tk, L.tv,
+                                                                               L.p);
   return static_cast<int>(cudaGetLastError());
+}
+
+long long ring_state_floats(int batch, int heads, int seg_len, int q_nseg) {
+  const long long tiles_per_seg = (seg_len + kBlockN - 1) / kBlockN;
+  return static_cast<long long>(batch) * heads * tiles_per_seg * q_nseg * kStateFloatsPerTile;
 }
 
 }  // namespace
@@ -736,4 +796,66 @@ extern "C" int erd_attn_fwd_cross_bf16(
   for (int b = 0; b < kMaxCrossBatch; ++b)
     L.p.kv_valid[b] = b < batch ? (kv_valid != nullptr ? kv_valid[b] : kv_len) : 0;
   return launch<false>(L, static_cast<unsigned>((L.p.q_tiles + 1) / 2), heads, batch, stream);
+}
+
+extern "C" size_t erd_ring_state_bytes(int batch, int heads, int seg_len, int q_nseg) {
+  if (batch <= 0 || heads <= 0 || seg_len <= 0 || q_nseg <= 0 || q_nseg > kMaxSegments) return 0;
+  return static_cast<size_t>(ring_state_floats(batch, heads, seg_len, q_nseg)) * sizeof(float);
+}
+
+extern "C" int erd_attn_fwd_ring_bf16(
+    const void* q, const void* k, const void* v, int64_t q_token_stride, int64_t q_head_stride,
+    int64_t q_batch_stride, int64_t q_seg_stride, int64_t k_token_stride, int64_t k_head_stride,
+    int64_t k_batch_stride, int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+    int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads, int seg_len, int q_nseg,
+    const int32_t* q_seg_lens, int kv_seg_len, int kv_nseg, const int32_t* kv_seg_lens,
+    int head_dim, float softmax_scale, void* out, int64_t o_token_stride, int64_t o_head_stride,
+    int64_t o_batch_stride, int64_t o_seg_stride, void* const* seg_out, void* state,
+    size_t state_bytes, int state_mode, int* status, void* stream) {
+  if (state_mode < 0 || state_mode > (kStateRead | kStateWrite)) return kErrBadShape;
+  const bool writes_output = (state_mode & kStateWrite) == 0;
+  if (kv_seg_lens == nullptr) return kErrNullPointer;
+  if (kv_nseg <= 0 || kv_nseg > kMaxSegments || q_nseg <= 0 || q_nseg > kMaxSegments ||
+      kv_seg_len <= 0)
+    return kErrBadShape;
+  for (int s = 0; s < kv_nseg; ++s)
+    if (kv_seg_lens[s] <= 0 || kv_seg_lens[s] > kv_seg_len) return kErrBadShape;
+  if (writes_output && out == nullptr && seg_out == nullptr) return kErrNullPointer;
+  if (seg_out != nullptr) {
+    for (int s = 0; s < q_nseg; ++s) {
+      if (seg_out[s] == nullptr) return kErrNullPointer;
+      if (!aligned16(seg_out[s])) return kErrMisaligned;
+    }
+  }
+  // The output pointer goes through the common checks; with the state written
+  // instead (or per-segment bases) it is never dereferenced.
+  const void* out_checked = out != nullptr ? out : (seg_out != nullptr ? seg_out[0] : q);
+  Launch L;
+  if (int rc = prepare(q, k, v, q_token_stride, q_head_stride, q_batch_stride, q_seg_stride,
+                       k_token_stride, k_head_stride, k_batch_stride, k_seg_stride,
+                       v_token_stride, v_head_stride, v_batch_stride, v_seg_stride, batch, heads,
+                       seg_len, q_nseg, q_seg_lens, head_dim, softmax_scale,
+                       const_cast<void*>(out_checked), o_token_stride, o_head_stride,
+                       o_batch_stride, o_seg_stride, status, &L))
+    return rc;
+  if (make_operand_map(&L.tk, k, kv_seg_len, heads, batch, kv_nseg, k_token_stride,
+                       k_head_stride, k_batch_stride, k_seg_stride) ||
+      make_operand_map(&L.tv, v, kv_seg_len, heads, batch, kv_nseg, v_token_stride,
+                       v_head_stride, v_batch_stride, v_seg_stride))
+    return kErrTensorMap;
+  const long long kv_tiles_per_seg = (kv_seg_len + kBlockN - 1) / kBlockN;
+  if (kv_tiles_per_seg * kv_nseg > (1LL << 24)) return kErrTooLarge;
+  L.p.kv_tiles_per_seg = static_cast<int>(kv_tiles_per_seg);
+  L.p.kv_tiles = static_cast<int>(kv_tiles_per_seg * kv_nseg);
+  for (int s = 0; s < kMaxSegments; ++s) L.p.kv_seg_lens[s] = s < kv_nseg ? kv_seg_lens[s] : 0;
+  if (seg_out != nullptr)
+    for (int s = 0; s < q_nseg; ++s) L.p.seg_out[s] = static_cast<__nv_bfloat16*>(seg_out[s]);
+  const unsigned ctas = static_cast<unsigned>((L.p.q_tiles + 1) / 2);
+  if (state_mode == 0) return launch<false>(L, ctas, heads, batch, stream);
+  if (state == nullptr) return kErrNullPointer;
+  if (!aligned16(state)) return kErrMisaligned;
+  if (state_bytes < erd_ring_state_bytes(batch, heads, seg_len, q_nseg)) return kErrTooLarge;
+  L.p.state = static_cast<float*>(state);
+  L.p.state_mode = state_mode;
+  return launch<false, true>(L, ctas, heads, batch, stream);
 }

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define ERD_ABI_VERSION 3
+#define ERD_ABI_VERSION 4
 
 /* ABI version probe; replaces eraserdit_mask_sta_abi()
  * (layers/attention/backends/csrc/mask_sta/core.cu:767). */
@@ -135,6 +135,39 @@ int erd_attn_fwd_cross_bf16(
     int q_len, int kv_len, const int32_t* kv_valid, int head_dim, float softmax_scale, void* out,
     int64_t o_token_stride, int64_t o_head_stride, int64_t o_batch_stride, int* status,
     void* stream);
+
+/*
+ * Ring (USP) attention, head_dim 64.  Serves the ring axis of
+ * DistributedSequenceRank.attention (models/adapters/eraserdit/nccl_sequence.py:
+ * 235-332) and replaces ring_accumulator.piece (layers/attention/
+ * ring_accumulator.py:12-100).  The queries are q_nseg segments (q_seg_lens
+ * valid tokens each, slots of seg_len tokens) and the keys / values kv_nseg
+ * segments (kv_seg_lens valid tokens each, slots of kv_seg_len tokens); the
+ * length arrays are host arrays and the strides those of erd_attn_fwd_bf16.
+ *   - state_mode 0: one launch over every key segment (the reference's
+ *     "reference" ring mode, after its ring gather of K/V shards);
+ *   - otherwise one launch per ring piece with a carried softmax state
+ *     (the "streaming" mode): bit 1 (read) starts from `state`, bit 2 (write)
+ *     stores the state instead of the output.  First piece: 2; middle: 3;
+ *     last: 1 (writes the BF16 output).  `state` is caller-owned device
+ *     memory, 16-byte aligned, of erd_ring_state_bytes(batch, heads, seg_len,
+ *     q_nseg) bytes; it holds O (fp32, unnormalised) and the running max / sum
+ *     of every query row.  Pieces of one state run in stream order.
+ * seg_out (host array of q_nseg device pointers, or NULL) replaces
+ * out + s * o_seg_stride as the output base of query segment s.  out may be
+ * NULL when seg_out is given or the state is written.  Returns -6 when
+ * state_bytes is too small.
+ */
+size_t erd_ring_state_bytes(int batch, int heads, int seg_len, int q_nseg);
+int erd_attn_fwd_ring_bf16(
+    const void* q, const void* k, const void* v, int64_t q_token_stride, int64_t q_head_stride,
+    int64_t q_batch_stride, int64_t q_seg_stride, int64_t k_token_stride, int64_t k_head_stride,
+    int64_t k_batch_stride, int64_t k_seg_stride, int64_t v_token_stride, int64_t v_head_stride,
+    int64_t v_batch_stride, int64_t v_seg_stride, int batch, int heads, int seg_len, int q_nseg,
+    const int32_t* q_seg_lens, int kv_seg_len, int kv_nseg, const int32_t* kv_seg_lens,
+    int head_dim, float softmax_scale, void* out, int64_t o_token_stride, int64_t o_head_stride,
+    int64_t o_batch_stride, int64_t o_seg_stride, void* const* seg_out, void* state,
+    size_t state_bytes, int state_mode, int* status, void* stream);
 
 /*
  * Block-sparse variant of erd_attn_fwd_bf16 for the mask-aware pattern.

@@ -40,3 +40,13 @@ def test_binding_covers_header_and_version(lib):
     assert lib.erd_abi_version() == _native.ABI_VERSION
     lib.erd_error_string.restype = ctypes.c_char_p
     assert lib.erd_error_string(-3).decode().startswith("pointer or stride")
+
+
+def test_ring_state_size(lib):
+    """Per query tile of 128 rows: 64 fp32 O columns plus the running max and
+    sum; tiles = ceil(seg_len / 128) per query segment."""
+    lib.erd_ring_state_bytes.restype = ctypes.c_size_t
+    assert lib.erd_ring_state_bytes(2, 16, 4080, 2) == 2 * 16 * (32 * 2) * (64 * 128 + 2 * 128) * 4
+    assert lib.erd_ring_state_bytes(1, 1, 1, 1) == (64 * 128 + 2 * 128) * 4
+    assert lib.erd_ring_state_bytes(0, 16, 4080, 2) == 0
+    assert lib.erd_ring_state_bytes(1, 16, 4080, 17) == 0
