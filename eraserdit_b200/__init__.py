@@ -9,6 +9,7 @@ for the C ABI underneath):
 - :mod:`eraserdit_b200.rotary` -- ``LTXVideoRotaryPosEmbed`` (factored table)
 - :mod:`eraserdit_b200.layer` -- ``EraserDiTSelfAttention`` (one ``attn1``)
 - :mod:`eraserdit_b200.ulysses` -- Ulysses SP (peer-memory or NCCL exchange, head chunks)
+- :mod:`eraserdit_b200.ring` -- ring and Ulysses x Ring SP, ``piece`` (ring accumulator)
 - :mod:`eraserdit_b200.topology`, :mod:`eraserdit_b200.sequence_sharding` -- CFG / SP groups
   and shard plans
 - :mod:`eraserdit_b200.mask_sta`, :mod:`eraserdit_b200.sparse_pattern` -- mask-aware
