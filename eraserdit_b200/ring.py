@@ -447,8 +447,9 @@ def emulate_usp_ranks(layer: EraserDiTSelfAttention, ulysses: int, ring: int, x:
             for dst, src in zip(pairs[idx][1], sends):
                 dst.copy_(src)
 
-    for usp, s in zip(ranks, steps):
-        usp.effective_attention = mode
+    label = "b200_ring_gather" if mode == "reference" else "b200_ring_fp32_state"
+    for usp in ranks:
+        usp.effective_attention = label
     if mode == "reference":
         for hop in range(ring - 1):
             rotate_all(hop)
