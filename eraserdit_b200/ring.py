@@ -170,7 +170,9 @@ class UspSelfAttention(UlyssesSelfAttention):
         self.sp_rank = rank + degree * ring_rank
         self._usp: dict[tuple, tuple] = {}
         self.calls_ring = 0
+        # diagnostics of the reference's rank object (nccl_sequence.py:19-20,262,274,281)
         self.effective_attention = None
+        self.partial_attention_dtype = None
 
     # ------------------------------------------------------------ partition
     def _bounds(self, length: int, rank: int) -> tuple[int, int]:
@@ -340,6 +342,7 @@ class UspSelfAttention(UlyssesSelfAttention):
             attend(None)
         elif not step.send1.is_cuda or R == 1:
             self.effective_attention = "b200_ring_fp32_state"
+            self.partial_attention_dtype = "float32_carried_state"
             for hop in range(R):
                 attend(hop)
                 if hop + 1 < R:
@@ -347,6 +350,7 @@ class UspSelfAttention(UlyssesSelfAttention):
                     self.calls_ring += 1
         else:
             self.effective_attention = "b200_ring_fp32_state"
+            self.partial_attention_dtype = "float32_carried_state"
             self._streaming_overlapped(step, attend)
         step.send2[0, :, :FLAG].fill_(0.0 if error is None else 1.0)
         self.calls += 1
