@@ -369,8 +369,10 @@ class UlyssesSelfAttention:
         if bufs is None:
             lengths = self._lengths(length)
             hl = self.local_heads
+            # recv2 is the output projection's input, [b][token slot][src][hl][d]:
+            # every source's rows land in place, no head gather follows.
             sizes = {"recv1": 2 * self.degree * max(lengths) * 3 * batch * hl * HEAD_DIM,
-                     "recv2": 2 * self.degree * lengths[self.rank] * batch * hl * HEAD_DIM}
+                     "recv2": 2 * batch * max(lengths) * self.degree * hl * HEAD_DIM}
             bufs = PeerBuffers(sizes, torch.device(device))
             if connect:
                 bufs.connect_group(self.group, self.rank, self.degree)
@@ -438,9 +440,10 @@ class UlyssesSelfAttention:
         stream = _native.stream_handle(device)
         status = _native.status_word(device)
         wait(bufs, PHASE_IN, n, self._epoch, status, stream)
-        row1, qkv_gap, row2 = 3 * batch * hl * HEAD_DIM, batch * hl * HEAD_DIM, batch * hl * HEAD_DIM
+        row1, qkv_gap = 3 * batch * hl * HEAD_DIM, batch * hl * HEAD_DIM
         base = bufs.local["recv1"]
-        seg_out = (ctypes.c_void_p * n)(*[bufs.peers["recv2"][s] + 2 * self.rank * lengths[s] * row2
+        # this rank's heads of every owner's tokens: owner s's recv2[b][token][self.rank]
+        seg_out = (ctypes.c_void_p * n)(*[bufs.peers["recv2"][s] + 2 * self.rank * hl * HEAD_DIM
                                           for s in range(n)])
         lens = (ctypes.c_int32 * n)(*lengths)
         strides = (row1, HEAD_DIM, hl * HEAD_DIM, lmax * row1)
@@ -451,7 +454,7 @@ class UlyssesSelfAttention:
             e0.record()
         common = (base, base + 2 * qkv_gap, base + 4 * qkv_gap, *strides, *strides, *strides,
                   batch, hl, lmax, n, lens, HEAD_DIM, float(self.layer.softmax_scale), seg_out,
-                  row2, HEAD_DIM, hl * HEAD_DIM)
+                  n * hl * HEAD_DIM, HEAD_DIM, lmax * n * hl * HEAD_DIM)
         with torch.cuda.device(device):
             if self.sparse is not None:
                 plan = self._sparse_segments.get(sum(lengths))  # keyed by sequence length
@@ -492,10 +495,9 @@ class UlyssesSelfAttention:
         event = torch.cuda.Event()
         event.record()
         self._pending = (event, host, bufs, self._epoch, n)
-        lme = lengths[self.rank]
-        heads = bufs.view("recv2", n * lme * batch * hl * HEAD_DIM, torch.bfloat16)
-        attn = heads.view(n, lme, batch, hl, HEAD_DIM).permute(2, 1, 0, 3, 4)
-        return self.layer.project_out(attn.reshape(batch, lme, n * hl * HEAD_DIM))
+        lme, lmax = lengths[self.rank], max(lengths)
+        heads = bufs.view("recv2", batch * lmax * n * hl * HEAD_DIM, torch.bfloat16)
+        return self.layer.project_out(heads.view(batch, lmax, n * hl * HEAD_DIM)[:, :lme])
 
     def _forward_peer(self, x_local: torch.Tensor, rope, length: int) -> torch.Tensor:
         self.drain()  # the previous call's status (normally complete by now)
