@@ -58,12 +58,14 @@ def test_head_chunks_bitwise_equal_unchunked(degree, chunks):
         assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("degree", [2, 4, 8])
-def test_peer_transport_bitwise_equal_nccl_layout(degree):
+@pytest.mark.parametrize("degree,grid", [(2, (2, 8, 12)), (4, (2, 8, 12)), (8, (2, 8, 12)),
+                                         (2, (1, 7, 11)), (4, (1, 7, 11)), (8, (3, 5, 7))])
+def test_peer_transport_bitwise_equal_nccl_layout(degree, grid):
     """The peer-memory exchange (prologue and attention epilogue storing into
-    the peers' buffers) gives exactly the all-to-all path's result."""
+    the peers' buffers, rows landing in the output projection's input layout)
+    gives exactly the all-to-all path's result, with even and uneven shards."""
     from eraserdit_b200.ulysses import emulate_ranks
-    layer, rope, x = _setup(2, 8, 12, 2, seed=10 + degree)
+    layer, rope, x = _setup(*grid, 2, seed=10 + degree)
     nccl = emulate_ranks(layer, degree, x, rope)
     peer = emulate_ranks(layer, degree, x, rope, transport="peer")
     for a, b in zip(nccl, peer):
