@@ -4,9 +4,13 @@
     python -m eraserdit_b200.profile_case prologue --batch 2 --seq 32640 --iters 3
     python -m eraserdit_b200.profile_case fp8 --batch 1 --seq 16320 --iters 3
     python -m eraserdit_b200.profile_case sparse --batch 1 --heads 16 --iters 3
+    python -m eraserdit_b200.profile_case ring --batch 1 --seq 16320 --iters 2
 
 ``sparse`` runs the configuration-4 pattern (32640 tokens in tile order, the
-seeded ellipse mask) whatever ``--seq`` says.
+seeded ellipse mask) whatever ``--seq`` says.  ``ring`` attends ``--seq``
+queries to two ring pieces of ``--seq`` keys each with the carried state (the
+per-rank work of ring degree 2): per iteration, one launch writing the state
+and one reading it and writing the output.
 
 Each runs the named kernel ``iters`` times on seeded inputs (sized above L2 by
 default) and exits 0, so that an ncu capture (``-k``/``-c``) of one to three
@@ -22,7 +26,7 @@ import torch
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["attention", "prologue", "fp8", "sparse"])
+    ap.add_argument("kernel", choices=["attention", "prologue", "fp8", "sparse", "ring"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seq", type=int, default=16320)
     ap.add_argument("--heads", type=int, default=32)
@@ -32,7 +36,15 @@ def main() -> None:
     torch.cuda.set_device(device)
     g = torch.Generator(device=device).manual_seed(0)
     from eraserdit_b200 import _native
-    if args.kernel in ("attention", "fp8", "sparse"):
+    if args.kernel == "ring":
+        from eraserdit_b200.ring import piece
+        mk = lambda: torch.randn(args.batch, args.seq, args.heads, 64, generator=g,
+                                 device=device).bfloat16()
+        q, k0, v0, k1, v1 = mk(), mk(), mk(), mk(), mk()
+        for _ in range(args.iters):
+            state = piece(q, k0, v0, scale=0.125)
+            piece(q, k1, v1, state, final=True, scale=0.125)
+    elif args.kernel in ("attention", "fp8", "sparse"):
         from eraserdit_b200.attention import attention_bshd
         plan = None
         if args.kernel == "sparse":
