@@ -111,3 +111,15 @@ def test_probe_and_rejections():
         _impl().forward(q, k, v, AttentionMetadata(attn_mask=torch.ones(1, dtype=torch.bool)))
     with pytest.raises(ValueError):
         _impl().forward(q.float(), k.float(), v.float(), AttentionMetadata())
+
+
+@pytest.mark.parametrize("batch,seq", [(2, 0), (0, 16)])
+def test_empty_inputs_return_empty_output(batch, seq):
+    """An empty sequence or batch gives an empty output (as the reference's
+    SDPA does) and launches nothing."""
+    from eraserdit_b200 import _native
+    from eraserdit_b200.attention import AttentionMetadata
+    q = torch.empty(batch, seq, 4, 64, device="cuda", dtype=torch.bfloat16)
+    out = _impl().forward(q, q, q, AttentionMetadata())
+    assert out.shape == q.shape and out.dtype == torch.bfloat16
+    assert _native.read_status(q.device) == 0
