@@ -54,7 +54,7 @@ def run_sequence_parallel(args) -> None:
         x_full = torch.randn(B.BATCH, B.SEQ, B.HIDDEN, generator=g, device=device).bfloat16()
         per_branch = B.BATCH // cfg
         x_branch = x_full[cfg_index * per_branch:(cfg_index + 1) * per_branch]
-        transport = args.transport if ring == 1 else "nccl"
+        transport = args.transport
 
         def make_layer():
             if ring > 1:
@@ -62,7 +62,7 @@ def run_sequence_parallel(args) -> None:
                 return UspSelfAttention(layer, len(ranks), index,
                                         peer_exchange(group, ranks, index), ring, rindex,
                                         ring_rotate(rgroup, rranks, rindex), group_ranks=ranks,
-                                        mode=args.ring_mode)
+                                        mode=args.ring_mode, transport=transport, group=group)
             return UlyssesSelfAttention(layer, len(ranks), index,
                                         peer_exchange(group, ranks, index), group_ranks=ranks,
                                         sparse=plan, head_chunks=args.head_chunks,

@@ -152,8 +152,9 @@ class UspSelfAttention(UlyssesSelfAttention):
 
     def __init__(self, layer: EraserDiTSelfAttention, degree: int, rank: int, exchange,
                  ring_degree: int, ring_rank: int, rotate, group_ranks=None,
-                 mode: str = "reference") -> None:
-        super().__init__(layer, degree, rank, exchange, group_ranks=group_ranks, head_chunks=1)
+                 mode: str = "reference", transport: str = "nccl", group=None) -> None:
+        super().__init__(layer, degree, rank, exchange, group_ranks=group_ranks, head_chunks=1,
+                         transport=transport, group=group)
         if mode not in RING_MODES:
             raise ValueError(f"ring mode must be one of {RING_MODES}")
         if layer.precision != "bf16":
@@ -169,6 +170,7 @@ class UspSelfAttention(UlyssesSelfAttention):
         self.sp_degree = degree * ring_degree
         self.sp_rank = rank + degree * ring_rank
         self._usp: dict[tuple, tuple] = {}
+        self._peer_state: dict[tuple, RingState] = {}
         self.calls_ring = 0
         # diagnostics of the reference's rank object (nccl_sequence.py:19-20,262,274,281)
         self.effective_attention = None
@@ -196,6 +198,14 @@ class UspSelfAttention(UlyssesSelfAttention):
     def chunks_for(self, length: int) -> int:
         return 1
 
+    def _slots(self) -> int:
+        """K/V piece slots: every piece (reference mode) or two (streaming)."""
+        return self.ring_degree if self.mode == "reference" else min(2, self.ring_degree)
+
+    def _exchange_slot(self) -> int:
+        """The slot the Ulysses exchange fills with this ring index's piece."""
+        return self.ring_rank if self.mode == "reference" else 0
+
     # -------------------------------------------------------------- buffers
     def _usp_buffers(self, batch: int, length: int, device, dtype):
         key = (batch, length, str(device), dtype)
@@ -206,7 +216,7 @@ class UspSelfAttention(UlyssesSelfAttention):
             lmax = max(floor_lengths(length, self.sp_degree))
             row = batch * hl * HEAD_DIM
             lme = lengths[self.rank]
-            slots = self.ring_degree if self.mode == "reference" else min(2, self.ring_degree)
+            slots = self._slots()
             send1 = torch.empty(3, n, lme, row, device=device, dtype=dtype)
             # Zeroed once: slot rows past a shorter source's tokens stay finite
             # (zero V rows times zero weights).
@@ -270,7 +280,7 @@ class UspSelfAttention(UlyssesSelfAttention):
     def ulysses_in(self, step: _Step) -> list[tuple[list, list]]:
         """(outputs, inputs) of the three Ulysses exchanges (Q, K, V)."""
         n = self.degree
-        slot = self.ring_rank if self.mode == "reference" else 0
+        slot = self._exchange_slot()
         targets = (step.recv1, step.kbuf[slot], step.vbuf[slot])
         return [([targets[i][s, :step.lengths[s]] for s in range(n)],
                  [step.send1[i, d] for d in range(n)]) for i in range(3)]
@@ -293,11 +303,18 @@ class UspSelfAttention(UlyssesSelfAttention):
         n, b, hl = self.degree, step.batch, self.local_heads
         row, lmax = b * hl * HEAD_DIM, step.lmax
         strides = (row, HEAD_DIM, hl * HEAD_DIM, lmax * row)
-        o = step.send2[0].view(-1)[FLAG:]
-        o_strides = (row, HEAD_DIM, hl * HEAD_DIM, FLAG + lmax * row)
+        seg_out = getattr(step, "seg_out", None)
+        if seg_out is not None:
+            # peer transport: rows straight into the owners' output-projection
+            # input, recv2[b][token slot][src][head][d]
+            o = None
+            o_strides = (n * hl * HEAD_DIM, HEAD_DIM, lmax * n * hl * HEAD_DIM, 0)
+        else:
+            o = step.send2[0].view(-1)[FLAG:]
+            o_strides = (row, HEAD_DIM, hl * HEAD_DIM, FLAG + lmax * row)
         common = dict(batch=b, heads=hl, seg_len=lmax, q_seg_lens=step.lengths, kv_seg_len=lmax,
                       q_strides=strides, k_strides=strides, v_strides=strides,
-                      o_strides=o_strides)
+                      o_strides=o_strides, seg_out=seg_out)
         if hop is None:
             kv_lens = floor_lengths(step.length, self.sp_degree)
             ring_attention_into(step.recv1, step.kbuf, step.vbuf, o, self.layer.softmax_scale,
@@ -340,7 +357,7 @@ class UspSelfAttention(UlyssesSelfAttention):
                 self.rotate(*self.ring_pairs(step, hop))
                 self.calls_ring += 1
             attend(None)
-        elif not step.send1.is_cuda or R == 1:
+        elif not step.recv1.is_cuda or R == 1:
             self.effective_attention = "b200_ring_fp32_state"
             self.partial_attention_dtype = "float32_carried_state"
             for hop in range(R):
@@ -352,7 +369,6 @@ class UspSelfAttention(UlyssesSelfAttention):
             self.effective_attention = "b200_ring_fp32_state"
             self.partial_attention_dtype = "float32_carried_state"
             self._streaming_overlapped(step, attend)
-        step.send2[0, :, :FLAG].fill_(0.0 if error is None else 1.0)
         self.calls += 1
         if error is not None:
             step.failed = True
@@ -362,7 +378,7 @@ class UspSelfAttention(UlyssesSelfAttention):
         """Piece ``hop`` attends on the current stream while piece ``hop + 1``
         rotates on a communication stream; a slot is received into only after
         the attention that read it has finished."""
-        device = step.send1.device
+        device = step.recv1.device
         current = torch.cuda.current_stream(device)
         if self._comm_stream is None:
             self._comm_stream = torch.cuda.Stream(device=device)
@@ -400,15 +416,136 @@ class UspSelfAttention(UlyssesSelfAttention):
             self.ring_attention(step)
         except Exception as exc:  # every rank still enters the inverse exchange
             error = exc
+        step.send2[0, :, :FLAG].fill_(0.0 if error is None else 1.0)
         self.exchange(*self.send_recv_2(step))
         if error is not None:
             raise error
 
     def forward(self, x_local: torch.Tensor, rope, length: int) -> torch.Tensor:
         """Layer output for this rank's tokens [B, L_rank, 2048]."""
+        if self.transport == "peer":
+            self.drain()  # the previous call's status (normally complete by now)
+            step = self.usp_peer_pre(x_local, rope, length)
+            self.usp_peer_wait_in(step)
+            ok = True
+            try:
+                self.ring_attention(step)
+            except Exception:  # every rank still signals and waits
+                ok = False
+            self.usp_peer_signal_out(step, ok)
+            return self.usp_peer_post(step, ok)
         step = self.pre(x_local, rope, length)
         self._run(step)
         return self.post(step)
+
+    # ----------------------------------------------------- peer transport
+    # The Ulysses exchanges become stores over NVLink (CUDA IPC mappings inside
+    # the Ulysses group): the prologue stores Q, K and V into the group peers'
+    # recv1 (``recv_q``, and the K / V piece slot this ring index fills), the
+    # last attention launch stores rows into the owners' recv2, and the epoch
+    # flags of ``peer_exchange`` order the two phases.  The rotation stays a
+    # batch of NCCL sends and receives over the ring group.  A rank passes the
+    # second wait of call k only after every group peer's rotations and
+    # attention of call k (which read and receive into its recv1) are done.
+
+    def peer_buffers(self, batch: int, length: int, device, connect=True):
+        from .peer_exchange import PeerBuffers
+        key = (batch, length, str(device))
+        bufs = self._peer.get(key)
+        if bufs is None:
+            n, hl = self.degree, self.local_heads
+            lmax = max(floor_lengths(length, self.sp_degree))
+            row = batch * hl * HEAD_DIM
+            # recv1 = recv_q [src][slot token][row] | kbuf [slot][src][...] | vbuf [...];
+            # recv2 = [b][token slot][src][head][d], the output projection's input
+            sizes = {"recv1": 2 * (1 + 2 * self._slots()) * n * lmax * row,
+                     "recv2": 2 * batch * lmax * n * hl * HEAD_DIM}
+            bufs = PeerBuffers(sizes, torch.device(device))  # zero-filled
+            if connect and self.degree == 1:
+                bufs.connect_local([bufs])  # a one-rank Ulysses group stores locally
+            elif connect:
+                bufs.connect_group(self.group, self.rank, self.degree)
+            self._peer[key] = bufs
+        return bufs
+
+    def _peer_step(self, bufs, batch: int, length: int) -> _Step:
+        n, hl = self.degree, self.local_heads
+        lengths = self._lengths(length)
+        lmax = max(floor_lengths(length, self.sp_degree))
+        row = batch * hl * HEAD_DIM
+        slots = self._slots()
+        region = bufs.view("recv1", (1 + 2 * slots) * n * lmax * row, torch.bfloat16)
+        recv_q = region[:n * lmax * row].view(n, lmax, row)
+        kbuf = region[n * lmax * row:(1 + slots) * n * lmax * row].view(slots, n, lmax, row)
+        vbuf = region[(1 + slots) * n * lmax * row:].view(slots, n, lmax, row)
+        state = self._peer_state.get((batch, length))
+        if state is None and self.mode != "reference" and self.ring_degree > 1:
+            state = self._peer_state[(batch, length)] = RingState(batch, hl, lmax, n, bufs.device)
+        start, _ = self._bounds(length, self.rank)
+        step = _Step(batch, length, lengths, start, None, recv_q, None, None)
+        step.kbuf, step.vbuf, step.state, step.lmax = kbuf, vbuf, state, lmax
+        step.bufs = bufs
+        step.seg_out = [bufs.peers["recv2"][s] + 2 * self.rank * hl * HEAD_DIM for s in range(n)]
+        return step
+
+    def usp_peer_pre(self, x_local: torch.Tensor, rope, length: int) -> _Step:
+        """QKV projection, then the prologue stores Q/K/V into the group peers' recv1."""
+        from .operator_fusion import qk_norm_rope_peer_into
+        from .peer_exchange import PHASE_IN, signal
+        batch = x_local.shape[0]
+        n, hl = self.degree, self.local_heads
+        start, end = self._bounds(length, self.rank)
+        if x_local.shape[1] != end - start:
+            raise ValueError("local sequence length must match the rank's partition")
+        bufs = self.peer_buffers(batch, length, x_local.device)
+        step = self._peer_step(bufs, batch, length)
+        self._epoch += 1
+        qkv = self.layer.project_qkv(x_local)
+        q, k, v = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN], qkv[..., 2 * HIDDEN:]
+        row, lmax, slots = batch * hl * HEAD_DIM, step.lmax, self._slots()
+        piece = n * lmax * row  # elements of one Q block or one K/V slot
+        slot = self._exchange_slot()
+        # our rows in destination d: recv_q[src = this rank], K / V in slot `slot`
+        dest = [bufs.peers["recv1"][d] + 2 * self.rank * lmax * row for d in range(n)]
+        qk_norm_rope_peer_into(q, k, v, self.layer.norm_q, self.layer.norm_k, self.layer.eps,
+                               rope, dest, piece * (1 + slot), piece * (1 + slots + slot),
+                               token_offset=start, out_token_stride=row,
+                               out_batch_stride=hl * HEAD_DIM, out_head_stride=HEAD_DIM,
+                               heads_per_dest=hl)
+        signal(bufs, PHASE_IN, self.rank, n, self._epoch, _native.stream_handle(x_local.device))
+        return step
+
+    def usp_peer_wait_in(self, step: _Step) -> None:
+        from .peer_exchange import PHASE_IN, wait
+        device = step.bufs.device
+        wait(step.bufs, PHASE_IN, self.degree, self._epoch, _native.status_word(device),
+             _native.stream_handle(device))
+
+    def usp_peer_signal_out(self, step: _Step, ok: bool) -> None:
+        from .peer_exchange import PHASE_OUT, signal
+        signal(step.bufs, PHASE_OUT, self.rank, self.degree, self._epoch if ok else -self._epoch,
+               _native.stream_handle(step.bufs.device))
+
+    def usp_peer_post(self, step: _Step, ok: bool) -> torch.Tensor:
+        """Wait for every group peer's rows, keep the status for drain(), project."""
+        from .peer_exchange import PHASE_OUT, wait
+        bufs, n, hl = step.bufs, self.degree, self.local_heads
+        device = bufs.device
+        word = _native.status_word(device)
+        wait(bufs, PHASE_OUT, n, self._epoch, word, _native.stream_handle(device))
+        if not ok:
+            raise RuntimeError("local sequence-parallel attention failed")
+        if self._status_host is None:
+            self._status_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+        host = self._status_host
+        host.copy_(word, non_blocking=True)
+        word.zero_()
+        event = torch.cuda.Event()
+        event.record()
+        self._pending = (event, host, bufs, self._epoch, n)
+        lme, lmax = step.lengths[self.rank], step.lmax
+        heads = bufs.view("recv2", step.batch * lmax * n * hl * HEAD_DIM, torch.bfloat16)
+        return self.layer.project_out(heads.view(step.batch, lmax, n * hl * HEAD_DIM)[:, :lme])
 
     def attention(self, query, key, value, impl=None, metadata=None) -> torch.Tensor:
         """The reference's SP hook with the ring axis (``nccl_sequence.py:235-332``)."""
@@ -427,17 +564,31 @@ class UspSelfAttention(UlyssesSelfAttention):
 
 
 def emulate_usp_ranks(layer: EraserDiTSelfAttention, ulysses: int, ring: int, x: torch.Tensor,
-                      rope, mode: str = "reference") -> list[torch.Tensor]:
+                      rope, mode: str = "reference", transport: str = "nccl"
+                      ) -> list[torch.Tensor]:
     """All U x R ranks of the USP layer in one process on one device
     (exchanges and rotations by copies, the same buffers and kernels as the
     NCCL path).  Returns each sequence-parallel rank's output, in rank order
     u + U * r."""
     length = x.shape[1]
-    ranks = [UspSelfAttention(layer, ulysses, u, None, ring, r, None, mode=mode)
+    ranks = [UspSelfAttention(layer, ulysses, u, None, ring, r, None, mode=mode,
+                              transport=transport)
              for r in range(ring) for u in range(ulysses)]
-    steps = [usp.pre(x[:, usp.partition(length)].contiguous(), rope, length) for usp in ranks]
     at = lambda u, r: ranks[u + ulysses * r]
-    for r in range(ring):  # Ulysses exchanges inside every ring index
+    if transport == "peer":
+        bufs = [usp.peer_buffers(x.shape[0], length, x.device, connect=False) for usp in ranks]
+        for r in range(ring):  # IPC-style mappings inside every Ulysses group
+            group = bufs[r * ulysses:(r + 1) * ulysses]
+            for b in group:
+                b.connect_local(group)
+        steps = [usp.usp_peer_pre(x[:, usp.partition(length)].contiguous(), rope, length)
+                 for usp in ranks]
+        for usp, s in zip(ranks, steps):
+            usp.usp_peer_wait_in(s)
+    else:
+        steps = [usp.pre(x[:, usp.partition(length)].contiguous(), rope, length)
+                 for usp in ranks]
+    for r in range(ring if transport != "peer" else 0):  # Ulysses exchanges per ring index
         for u in range(ulysses):
             for i, (outputs, _) in enumerate(at(u, r).ulysses_in(steps[u + ulysses * r])):
                 for src in range(ulysses):
@@ -465,6 +616,14 @@ def emulate_usp_ranks(layer: EraserDiTSelfAttention, ulysses: int, ring: int, x:
                 usp._ring_attend(s, hop)
             if hop + 1 < ring:
                 rotate_all(hop)
+    if transport == "peer":
+        for usp, s in zip(ranks, steps):
+            usp.usp_peer_signal_out(s, True)
+        outs = [usp.usp_peer_post(s, True) for usp, s in zip(ranks, steps)]
+        torch.cuda.synchronize(x.device)
+        for usp in ranks:
+            usp.close()  # raises a failed peer's error
+        return outs
     for usp, s in zip(ranks, steps):
         s.send2[0, :, :FLAG].zero_()
     for r in range(ring):  # inverse Ulysses exchanges

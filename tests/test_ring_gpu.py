@@ -114,3 +114,20 @@ def test_streaming_full_size_ring8():
     got = torch.cat(emulate_usp_ranks(layer, 1, 8, x, rope, mode="streaming"), dim=1)
     assert max_abs(got, want) <= 2e-2
     assert cosine(got, want) >= 0.99999
+
+
+@pytest.mark.parametrize("mode", ["reference", "streaming"])
+@pytest.mark.parametrize("ulysses,ring,grid", [(2, 2, (2, 8, 12)), (2, 2, (1, 7, 11)),
+                                               (4, 2, (3, 5, 7)), (2, 4, (2, 8, 12))])
+def test_peer_transport_bitwise_equal_nccl_layout(ulysses, ring, grid, mode):
+    """The peer-memory Ulysses exchanges inside every ring index (prologue and
+    last attention launch storing into the group peers' buffers) give exactly
+    the all-to-all layout's result, with even and uneven shards."""
+    from eraserdit_b200 import _native
+    from eraserdit_b200.ring import emulate_usp_ranks
+    layer, rope, x = _setup(*grid, 2, seed=3 * ulysses + ring)
+    nccl = emulate_usp_ranks(layer, ulysses, ring, x, rope, mode=mode)
+    peer = emulate_usp_ranks(layer, ulysses, ring, x, rope, mode=mode, transport="peer")
+    assert _native.read_status(x.device) == 0
+    for a, b in zip(nccl, peer):
+        assert torch.equal(a, b)

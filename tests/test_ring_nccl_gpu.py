@@ -2,7 +2,8 @@
 than 2): ring degree 2 (with Ulysses 2 on 4 GPUs, 4 on 8).  The reference ring
 mode equals the Ulysses layer at the same total degree bit for bit; the
 streaming mode (rotation on a second stream, carried state) matches the
-single-GPU layer's rows."""
+single-GPU layer's rows; the peer-memory Ulysses exchanges (CUDA IPC inside
+each Ulysses group) give the all-to-all result bit for bit."""
 import os
 import socket
 import tempfile
@@ -67,6 +68,17 @@ def _rank(rank, world, port, out_dir):
                 cos = float(torch.nn.functional.cosine_similarity(
                     got.float().flatten(), want[:, sl].float().flatten(), dim=0))
                 assert err <= 2e-2 and cos >= 0.99999, (mode, err, cos)
+                # the Ulysses exchanges as stores into the group peers' memory
+                peer = UspSelfAttention(layer, topo.ulysses, uindex,
+                                        peer_exchange(ug, uranks, uindex), ring, rindex,
+                                        ring_rotate(rg, rranks, rindex), group_ranks=uranks,
+                                        mode=mode, transport="peer", group=ug)
+                for _ in range(3):  # several epochs through the same buffers
+                    again = peer(x[:, usl].contiguous(), rope, length)
+                assert torch.equal(again, got), (mode, "peer transport differs")
+                torch.cuda.synchronize()
+                dist.barrier()
+                peer.close()
         torch.cuda.synchronize()
         open(os.path.join(out_dir, f"ok{rank}"), "w").close()
     finally:
