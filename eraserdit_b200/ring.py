@@ -30,6 +30,12 @@ of the sequence.  Per layer:
      that mode's merge approximates);
 4. output rows go to the Ulysses send buffer of their owners and return with
    the inverse exchange; heads are gathered and projected as in Ulysses.
+
+With ``transport="peer"`` steps 2 and 4 become stores over NVLink inside each
+Ulysses group, as on the Ulysses path: the prologue writes Q, K and V into the
+group peers' receive region, the last attention launch writes rows into the
+owners' output-projection input, and epoch flags order the phases; the
+rotation stays NCCL.
 """
 
 from __future__ import annotations
