@@ -204,6 +204,16 @@ class UspSelfAttention(UlyssesSelfAttention):
     def chunks_for(self, length: int) -> int:
         return 1
 
+    # The Ulysses object's single attention launch and its peer phases do not
+    # apply to the ring layout; the ring object has its own.
+    def _attend(self, step, chunk: int = 0) -> None:
+        raise TypeError("UspSelfAttention attends through ring_attention()")
+
+    def peer_pre(self, *args, **kwargs):
+        raise TypeError("UspSelfAttention's peer phases are usp_peer_pre/_wait_in/_signal_out/_post")
+
+    peer_attend = peer_post = peer_pre
+
     def _slots(self) -> int:
         """K/V piece slots: every piece (reference mode) or two (streaming)."""
         return self.ring_degree if self.mode == "reference" else min(2, self.ring_degree)
