@@ -50,3 +50,29 @@ def test_ring_state_size(lib):
     assert lib.erd_ring_state_bytes(1, 1, 1, 1) == (64 * 128 + 2 * 128) * 4
     assert lib.erd_ring_state_bytes(0, 16, 4080, 2) == 0
     assert lib.erd_ring_state_bytes(1, 16, 4080, 17) == 0
+
+
+def test_ring_entry_rejects_bad_arguments_before_any_device_call(lib):
+    """Argument errors of erd_attn_fwd_ring_bf16 come back as the documented
+    codes (-1 null pointer, -2 bad shape) before the device is touched."""
+    from eraserdit_b200 import _native
+    fn = lib.erd_attn_fwd_ring_bf16
+    fn.argtypes = _native.SIGNATURES["erd_attn_fwd_ring_bf16"]
+    fn.restype = ctypes.c_int
+    lens = (ctypes.c_int32 * 2)(100, 100)
+    big = (ctypes.c_int32 * 2)(100, 300)
+
+    def call(state_mode=0, kv_nseg=2, kv_lens=lens, q_nseg=2, kv_seg_len=128, out=1 << 20):
+        return fn(1 << 20, 1 << 20, 1 << 20, *([64] * 12), 1, 1, 128, q_nseg, lens, kv_seg_len,
+                  kv_nseg, kv_lens, 64, 0.125, out, 64, 64, 64, 64, None, None, 0, state_mode,
+                  None, None)
+
+    assert call(state_mode=4) == -2
+    assert call(state_mode=-1) == -2
+    assert call(kv_lens=None) == -1
+    assert call(kv_nseg=0) == -2
+    assert call(kv_nseg=17) == -2
+    assert call(q_nseg=0) == -2
+    assert call(kv_seg_len=0) == -2
+    assert call(kv_lens=big) == -2          # a segment longer than its slot
+    assert call(out=None) == -1             # BF16 output requested, no destination
