@@ -13,7 +13,7 @@ from tests.helpers import cosine, max_abs
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 sys.path.insert(0, str(GOLDEN))
-from make_golden_cross import TEXT_VALID, cross_inputs  # noqa: E402
+from make_golden_cross import cross_inputs  # noqa: E402
 
 ROWS = list(range(0, 192, 24)) + [191]
 

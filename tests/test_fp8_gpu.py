@@ -5,7 +5,7 @@ import pytest
 import torch
 
 from oracle import sage_fp8
-from tests.helpers import attention_fp32, cosine, max_abs
+from tests.helpers import attention_fp32, cosine
 
 pytestmark = pytest.mark.gpu
 

@@ -9,7 +9,6 @@ import os
 import socket
 import tempfile
 
-import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
