@@ -42,6 +42,17 @@ def test_binding_covers_header_and_version(lib):
     assert lib.erd_error_string(-3).decode().startswith("pointer or stride")
 
 
+def test_integration_binding_asserts_current_version():
+    """The ctypes stub a maintainer copies from INTEGRATION.md must accept the
+    library this repository builds (the version in the header and the binding)."""
+    from eraserdit_b200 import _native
+    text = (ROOT / "INTEGRATION.md").read_text()
+    asserted = [int(v) for v in re.findall(r"assert _lib\.erd_abi_version\(\) == (\d+)", text)]
+    assert asserted == [_native.ABI_VERSION]
+    header = (ROOT / "include" / "eraserdit_b200.h").read_text()
+    assert int(re.search(r"#define ERD_ABI_VERSION (\d+)", header).group(1)) == _native.ABI_VERSION
+
+
 def test_ring_state_size(lib):
     """Per query tile of 128 rows: 64 fp32 O columns plus the running max and
     sum; tiles = ceil(seg_len / 128) per query segment."""
