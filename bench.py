@@ -283,60 +283,74 @@ def build_sparse_plan(device):
 
 
 def run_e2e(call, host_x, host_y, device, warmup: int, steps: int) -> float:
-    """ms per step of host -> device copy, ``call``, device -> host copy, with
-    consecutive steps on two alternating streams (timed on the device)."""
-    current = torch.cuda.current_stream(device)
-    streams = [torch.cuda.Stream(device=device) for _ in range(2)]
+    """ms per step of: pinned host -> device copy of the step's input, ``call``
+    on the current stream, device -> pinned host copy of its output (timed on
+    the device).  The copies run on two copy streams with double-buffered
+    device inputs, so step i+1's upload and step i's download overlap the
+    kernels of the neighbouring steps; the layer itself runs on one stream."""
+    compute = torch.cuda.current_stream(device)
+    up, down = torch.cuda.Stream(device=device), torch.cuda.Stream(device=device)
+    xd = [torch.empty(host_x.shape, dtype=host_x.dtype, device=device) for _ in range(2)]
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
 
     def one(i):
-        s = streams[i % 2]
-        s.wait_stream(current)
-        with torch.cuda.stream(s):
-            host_y[i % 2].copy_(call(host_x.to(device, non_blocking=True)), non_blocking=True)
+        k = i % 2
+        up.wait_event(consumed[k])  # step i - 2 has finished with xd[k]
+        with torch.cuda.stream(up):
+            xd[k].copy_(host_x, non_blocking=True)
+            uploaded[k].record(up)
+        compute.wait_event(uploaded[k])
+        y = call(xd[k])
+        consumed[k].record(compute)
+        down.wait_event(consumed[k])
+        with torch.cuda.stream(down):
+            host_y[k].copy_(y, non_blocking=True)
+        y.record_stream(down)
 
     for i in range(max(warmup, 1)):
         one(i)
-    for s in streams:
-        current.wait_stream(s)
+    compute.wait_stream(down)
     torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(current)
+    start.record(compute)
+    up.wait_event(start)
     for i in range(steps):
-        s = streams[i % 2]
-        s.wait_event(start)
-        with torch.cuda.stream(s):
-            host_y[i % 2].copy_(call(host_x.to(device, non_blocking=True)), non_blocking=True)
-    for s in streams:
-        current.wait_stream(s)
-    stop.record(current)
+        one(i)
+    compute.wait_stream(down)
+    stop.record(compute)
     torch.cuda.synchronize()
     return start.elapsed_time(stop) / steps
 
 
-def run_single(args) -> None:
-    from eraserdit_b200 import _native
-    device = torch.device("cuda", 0)
-    torch.cuda.set_device(device)
-    precision = "fp8" if args.fp8 else "bf16"
-    layer, rope = build_problem(device, precision)
-    plan, kept, issued = build_sparse_plan(device) if args.sparse else (None, 1.0, 1.0)
-    if plan is not None:
-        rope = rope.in_order(plan.order)  # the sequence is laid out in tile order
-    g = torch.Generator(device=device).manual_seed(1)
-    x = torch.randn(BATCH, SEQ, HIDDEN, generator=g, device=device).bfloat16()
-    if args.qkv_fp8:
-        enable_qkv_fp8(layer, x)
-    stream = torch.cuda.current_stream(device)
-    attn_events = []
+def parity(got: torch.Tensor, want: torch.Tensor, vs: str, min_cosine: float,
+           max_abs: float | None = None) -> dict:
+    """Max-abs difference and cosine of two outputs, against the stated bars."""
+    g, w = got.float().flatten(), want.float().flatten()
+    err = float((g - w).abs().max()) if g.numel() else 0.0
+    cos = float(torch.nn.functional.cosine_similarity(g.double(), w.double(), dim=0))
+    ok = cos >= min_cosine and (max_abs is None or err <= max_abs)
+    bars = {"min_cosine": min_cosine}
+    if max_abs is not None:
+        bars["max_abs"] = max_abs
+    return {"vs": vs, "max_abs": err, "cosine": cos, "bars": bars, "ok": ok}
 
+
+def time_layer(layer, rope, x, plan, precision: str, steps: int, warmup: int, clocks=None):
+    """Device ms per layer step (the calls of ``EraserDiTSelfAttention.forward``)
+    and the attention kernel's mean ms from CUDA events around its launch on the
+    stream it is enqueued on.  Returns (ms, kernel_ms, last output)."""
     from eraserdit_b200.attention import attention_bshd
     from eraserdit_b200.mask_sta import sparse_attention_bshd
     from eraserdit_b200.operator_fusion import qk_norm_rope_into
-    attn_out = torch.empty(BATCH, SEQ, HIDDEN, device=device, dtype=torch.bfloat16)
+    device = x.device
+    stream = torch.cuda.current_stream(device)
+    attn_out = torch.empty(x.shape[0], x.shape[1], HIDDEN, device=device, dtype=torch.bfloat16)
+    if plan is not None:
+        rope = rope.in_order(plan.order)  # the sequence is laid out in tile order
+    events = []
 
     def step(record: bool):
-        # Same calls as EraserDiTSelfAttention.forward, with CUDA events around
-        # the attention kernel alone (on the stream it is launched on).
         qkv = layer.project_qkv(x)
         q, k, v = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN], qkv[..., 2 * HIDDEN:]
         qk_norm_rope_into(q, k, layer.norm_q, layer.norm_k, layer.eps, rope, q, k)
@@ -352,29 +366,102 @@ def run_single(args) -> None:
                            out=heads4(attn_out), precision=precision)
         if record:
             e1.record(stream)
-            attn_events.append((e0, e1))
+            events.append((e0, e1))
         return layer.project_out(attn_out)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step(False)
     torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(device.index) as clocks:
+    if clocks is not None:
+        clocks.__enter__()
+    try:
         start.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             y = step(True)
         stop.record(stream)
         torch.cuda.synchronize()
-    ms = start.elapsed_time(stop) / args.steps
-    core_ms = statistics.mean(a.elapsed_time(b) for a, b in attn_events)
+    finally:
+        if clocks is not None:
+            clocks.__exit__(None, None, None)
+    ms = start.elapsed_time(stop) / steps
+    kernel_ms = statistics.mean(a.elapsed_time(b) for a, b in events)
+    return ms, kernel_ms, y
+
+
+def protected_rows(plan, seq: int) -> torch.Tensor:
+    """Token positions (tile order) of the query blocks that attend every key."""
+    full = plan.blocks.all(dim=1).nonzero().flatten()
+    rows = (full[:, None] * 128 + torch.arange(128)[None, :]).flatten()
+    return rows[rows < seq]
+
+
+def extra_legs(device, x, rope, y_bf16, steps: int, warmup: int, peak_bf16: float,
+               peak_src: str) -> dict:
+    """Configurations 3 (FP8 attention numerics) and 4 (block-sparse) on one GPU,
+    each with its own device time, roofline and an output check."""
+    extra = {}
+    # FP8 attention (configuration 3's numerics) on the configuration-1 layer.
+    layer8, _ = build_problem(device, "fp8")
+    ms, kms, y = time_layer(layer8, rope, x, None, "fp8", steps, warmup)
+    achieved = ATTN_FLOP / (kms / 1e3) / 1e12
+    extra["fp8"] = {
+        "workload": "config 3 numerics on one GPU: FP8 (E4M3, per-128-token Q/K scales, "
+                    "smoothed K, per-channel V scales) attention in the config-1 layer, "
+                    "B=2 x 32640",
+        "ms_per_step": ms, "value": LAYER_FLOP / (ms / 1e3) / 1e12, "unit": UNIT,
+        "roofline": {"kernel": "attn_fwd_fp8 (+ fp8 quantize)", "bound": "tensor",
+                     "achieved": achieved, "peak": 2 * peak_bf16, "unit": UNIT,
+                     "frac": achieved / (2 * peak_bf16),
+                     "peak_source": f"{peak_src}: dense fp8 = 2 x bf16", "kernel_ms": kms},
+        "parity": parity(y, y_bf16, "the BF16 layer on the same input (north-star FP8 bar)",
+                         0.995),
+    }
+    del layer8, y
+    # Block-sparse attention (configuration 4); its protected query blocks
+    # attend every key, so their rows equal the dense layer's.
+    layer, rope1 = build_problem(device, "bf16")
+    plan, kept, issued = build_sparse_plan(device)
+    ms, kms, y = time_layer(layer, rope1, x, plan, "bf16", steps, warmup)
+    dense = layer(x, rope1.in_order(plan.order))
+    rows = protected_rows(plan, SEQ).to(device)
+    achieved = ATTN_FLOP * issued / (kms / 1e3) / 1e12
+    layer_flop = LINEAR_FLOP + ATTN_FLOP * kept
+    extra["sparse"] = {
+        "workload": SPARSE_WORKLOAD,
+        "ms_per_step": ms, "value": layer_flop / (ms / 1e3) / 1e12, "unit": UNIT,
+        "dense_equivalent": LAYER_FLOP / (ms / 1e3) / 1e12,
+        "kept_pair_fraction": kept, "issued_pair_fraction": issued,
+        "roofline": {"kernel": "attn_fwd_bf16 (block-sparse instantiation)", "bound": "tensor",
+                     "achieved": achieved, "peak": peak_bf16, "unit": UNIT,
+                     "frac": achieved / peak_bf16, "peak_source": peak_src, "kernel_ms": kms},
+        "parity": parity(y[:, rows], dense[:, rows],
+                         f"the dense BF16 layer on the {rows.numel()} rows of query blocks "
+                         "that attend every key", 0.99999, 1e-2),
+    }
+    return extra
+
+
+def run_single(args) -> None:
+    from eraserdit_b200 import _native
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    precision = "fp8" if args.fp8 else "bf16"
+    layer, rope = build_problem(device, precision)
+    plan, kept, issued = build_sparse_plan(device) if args.sparse else (None, 1.0, 1.0)
+    g = torch.Generator(device=device).manual_seed(1)
+    x = torch.randn(BATCH, SEQ, HIDDEN, generator=g, device=device).bfloat16()
+    if args.qkv_fp8:
+        enable_qkv_fp8(layer, x)
+    clocks = ClockSampler(device.index)
+    ms, core_ms, y = time_layer(layer, rope, x, plan, precision, args.steps, args.warmup,
+                                clocks=clocks)
     status = _native.read_status(device)
     if status:
         raise RuntimeError(f"kernel wait timed out (status {status})")
-    del y
 
     # End to end through the public API: pinned host input -> layer -> pinned host
-    # output, every step.  Consecutive steps alternate between two streams so that
-    # one step's copies (copy engines) overlap its neighbour's kernels.
+    # output, every step (copies on their own streams, overlapping the kernels).
     host_x = x.cpu().pin_memory()
     host_y = [torch.empty(BATCH, SEQ, HIDDEN, dtype=torch.bfloat16).pin_memory()
               for _ in range(2)]
@@ -385,6 +472,7 @@ def run_single(args) -> None:
     timed_s = ms * args.steps / 1e3
     peak_key = "bf16_tflops_sustained" if timed_s >= 1.0 else "bf16_tflops"
     peak = peaks[peak_key]
+    bf16_peak, bf16_src = peak, f"{peak_src} {peak_key}"
     if args.fp8:  # dense FP8 runs at twice the BF16 rate on this part
         peak, peak_key = 2 * peak, f"2 x {peak_key} (dense fp8 = 2x bf16)"
     # Sparse: algorithmic FLOPs are those of the kept pairs; the kernel's
@@ -421,7 +509,7 @@ def run_single(args) -> None:
                 "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": host_x.numel() * host_x.element_size(),
                 "d2h_bytes_per_step": host_y[0].numel() * host_y[0].element_size(),
-                "streams": 2},
+                "copy_streams": 2},
         "gpu_launches": ((4 if args.fp8 else 2) + (1 if args.qkv_fp8 else 0)) * args.steps,
         "clocks": clock,
     }
@@ -429,9 +517,19 @@ def run_single(args) -> None:
         line["sparsity"] = {"kept_pair_fraction": kept, "issued_pair_fraction": issued,
                             "dense_equivalent": LAYER_FLOP / (ms / 1e3) / 1e12,
                             "dense_equivalent_e2e": LAYER_FLOP / (e2e_ms / 1e3) / 1e12}
+    failed = []
+    if not (args.fp8 or args.sparse or args.qkv_fp8 or args.no_extra):
+        del host_x, host_y
+        line["extra"] = extra_legs(device, x, rope, y, min(args.steps, 10), args.warmup,
+                                   bf16_peak, bf16_src)
+        failed = [k for k, v in line["extra"].items() if not v["parity"]["ok"]]
+        if _native.read_status(device):
+            raise RuntimeError("kernel wait timed out in an extra leg")
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline()
     print(json.dumps(line), flush=True)
+    if failed:
+        raise SystemExit(f"output check failed: {failed}")
 
 
 def main() -> None:
@@ -441,6 +539,8 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", default="native", choices=["native", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-extra", action="store_true",
+                        help="skip the configuration-3/4 legs and the output checks")
     parser.add_argument("--cfg", type=int, default=1, help="CFG branches on separate rank groups")
     parser.add_argument("--fp8", action="store_true",
                         help="Sage-style FP8 attention (configuration 3) instead of BF16")

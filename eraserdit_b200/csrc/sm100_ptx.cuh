@@ -71,8 +71,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Wait for the phase with the given parity.  Returns false (after recording
-// `code` in *status and raising *abort) when the wait times out or another
-// role of the CTA has already aborted.
+// `code` in *status and raising *abort) when the wait times out, when another
+// role of the CTA has already aborted, or when the device status word already
+// holds an error (another CTA gave up): a failed launch then ends after one
+// timeout instead of one per CTA.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
                                           int* status, int code) {
   if (mbar_try_wait(bar, parity)) return true;
@@ -81,6 +83,10 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (*abort) return false;
+      if (status != nullptr && *reinterpret_cast<volatile int*>(status) != 0) {
+        *abort = 1;
+        return false;
+      }
       if (global_timer_ns() - t0 > kWaitTimeoutNs) {
         *abort = 1;
         if (status != nullptr) atomicOr(status, code);
