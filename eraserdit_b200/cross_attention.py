@@ -21,10 +21,10 @@ import ctypes
 from typing import Any
 
 import torch
-import torch.nn.functional as F
 
 from . import _native
 from .layer import HEAD_DIM, HIDDEN
+from .linear import linear_bf16
 
 CROSS_Q_RMSNORM_NATIVE_OP = "cross_q_rmsnorm_native"
 
@@ -142,12 +142,12 @@ class EraserDiTCrossAttention:
         batch, q_len, _ = hidden_states.shape
         kv_len = encoder_hidden_states.shape[1]
         kv_valid = mask_lengths(attention_mask, batch, kv_len)
-        q = rms_norm_rows(F.linear(hidden_states, self.wq, self.bq), self.norm_q, self.eps)
-        kvp = F.linear(encoder_hidden_states, self.w_kv, self.b_kv)  # [B, L, 4096]
+        q = rms_norm_rows(linear_bf16(hidden_states, self.wq, self.bq), self.norm_q, self.eps)
+        kvp = linear_bf16(encoder_hidden_states, self.w_kv, self.b_kv)  # [B, L, 4096]
         k = rms_norm_rows(kvp[..., :HIDDEN].contiguous(), self.norm_k, self.eps)
         v = kvp[..., HIDDEN:]
         heads4 = lambda t: t.unflatten(2, (self.heads, HEAD_DIM))
         core = cross_attention_bshd(heads4(q), heads4(k), heads4(v), self.scale, kv_valid)
-        return F.linear(core.flatten(2), self.wo, self.bo)
+        return linear_bf16(core.flatten(2), self.wo, self.bo)
 
     __call__ = forward

@@ -18,7 +18,7 @@ PACKAGE = CSRC.parent
 REPO = PACKAGE.parent
 LIBRARY = PACKAGE / "liberaserdit_b200.so"
 SOURCES = ["host_common.cu", "prologue.cu", "attention_bf16.cu", "attention_fp8.cu",
-           "attention_fp8_static.cu", "tokens.cu", "peer.cu", "quant.cu"]
+           "attention_fp8_static.cu", "tokens.cu", "peer.cu", "quant.cu", "linear.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -1,0 +1,338 @@
+// Linear layer y = x W^T + b on the sm_100a tensor cores: BF16 operands, FP32
+// accumulation in TMEM, bias added in FP32, BF16 output.
+//
+// Replaces the nn.Linear products of the reference's self-attention path:
+// the Q/K/V projections attn.to_q/to_k/to_v (models/dits/eraserdit_attention.py:
+// 248-253; nn.Linear(2048, 2048, bias=True), models/dits/eraserdit_transformer.py:
+// 253-263), run here as one product over the concatenated weights, and the
+// output projection to_out[0] (models/dits/eraserdit_attention.py:216-229).
+//
+// Design: a persistent kernel, one CTA per SM, walking 256 x 256 (or, for
+// problems with few tiles, 128 x 256) output tiles row-block major, so the
+// CTAs running at the same time share their rows of x and the whole weight
+// through L2.
+//   warp 0      TMA producer: 256 (128) x 64 tiles of x, 256 x 64 of W, through a ring of
+//               shared-memory stages (128-byte swizzle, K-major).
+//   warp 1      MMA issuer (one thread): two M=128 N=256 accumulators per tile
+//               (rows 0-127 and 128-255), K=16 per instruction, TMEM columns
+//               [0,256) and [256,512); with 128-row tiles one accumulator in
+//               each half of TMEM, alternating between tiles.
+//   warps 2-9   epilogue: each warp drains 32 rows x 256 (128) columns of one
+//               accumulator into registers (packed BF16 after the FP32 bias
+//               add), releases TMEM to the issuer, then stores its rows, so the
+//               next tile's products overlap the global stores.
+// Every wait is bounded; a timeout records a status bit and the CTA returns.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "host_common.h"
+#include "sm100_ptx.cuh"
+#include "tmem_io.cuh"
+
+namespace erd {
+namespace lin {
+
+// Loads 16 consecutive 32-bit TMEM columns of this thread's lane and waits for
+// them in the same asm statement.
+__device__ __forceinline__ void tmem_ld_wait_16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+constexpr int kBN = 256;  // output columns per tile (one N=256 product)
+constexpr int kBK = 64;   // K per stage: one 128-byte swizzle atom of BF16
+constexpr int kBBytes = kBN * kBK * 2;  // 32 KB
+constexpr int kEpilogueWarps = 8;
+constexpr int kThreads = 32 * (2 + kEpilogueWarps);
+
+// Tile geometry of the two instantiations: 256 output rows (two M=128
+// accumulators filling TMEM, 3 stages) or 128 rows (one accumulator, two TMEM
+// buffers so the epilogue of a tile overlaps the next tile's products, 4
+// stages) for problems whose 256-row tiles would leave SMs idle.
+template <int BM>
+struct Tile {
+  static constexpr int kAccs = BM / 128;     // M=128 accumulators per tile
+  static constexpr int kBufs = 2 / kAccs;    // TMEM tile buffers
+  static constexpr int kStages = BM == 128 ? 4 : 3;
+  static constexpr int kABytes = BM * kBK * 2;
+  static constexpr int kSmemA = 0;
+  static constexpr int kSmemB = kSmemA + kStages * kABytes;
+  static constexpr int kSmemBar = kSmemB + kStages * kBBytes;
+  static constexpr int kSmemLaunchBytes = kSmemBar + 1024 + 1024;  // + base alignment
+  static_assert(kSmemLaunchBytes <= 227 * 1024, "shared memory budget");
+};
+
+struct __align__(8) Barriers {
+  uint64_t full[4];
+  uint64_t empty[4];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t mma_drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+struct Params {
+  int m, n, k;
+  int tiles_m, tiles_n;
+  int a_rows;  // rows of the x tile box (BM, or m when m < BM)
+  const __nv_bfloat16* bias;  // [n] or null
+  __nv_bfloat16* c;
+  long long ldc;
+  int* status;
+};
+
+template <int BM>
+__global__ void __launch_bounds__(kThreads, 1)
+    linear_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                       const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+  using T = Tile<BM>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  Barriers* bars = reinterpret_cast<Barriers*>(smem + T::kSmemBar);
+  const uint32_t sA = smem_u32(smem + T::kSmemA);
+  const uint32_t sB = smem_u32(smem + T::kSmemB);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles = p.tiles_m * p.tiles_n;
+  const int ksteps = p.k / kBK;
+  volatile int* abort = &bars->abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < T::kStages; ++s) {
+      mbar_init(smem_u32(&bars->full[s]), 1);
+      mbar_init(smem_u32(&bars->empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&bars->acc_full[b]), 1);
+      mbar_init(smem_u32(&bars->acc_empty[b]), 32 * kEpilogueWarps);
+    }
+    mbar_init(smem_u32(&bars->mma_drain), 1);
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&bars->tmem_base), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_a);
+      tma_prefetch_desc(&tmap_b);
+      const uint32_t tx = static_cast<uint32_t>(p.a_rows * kBK * 2 + kBBytes);
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
+        const int m0 = (tile / p.tiles_n) * BM;
+        const int n0 = (tile % p.tiles_n) * kBN;
+        for (int kk = 0; kk < ksteps; ++kk, ++it) {
+          const int s = static_cast<int>(it % T::kStages);
+          const uint32_t ph = (it / T::kStages) & 1;
+          if (!mbar_wait(smem_u32(&bars->empty[s]), ph ^ 1, abort, p.status,
+                         kStatusTimeoutProducer))
+            break;
+          mbar_arrive_expect_tx(smem_u32(&bars->full[s]), tx);
+          tma_load_2d(sA + s * T::kABytes, &tmap_a, smem_u32(&bars->full[s]), kk * kBK, m0);
+          tma_load_2d(sB + s * kBBytes, &tmap_b, smem_u32(&bars->full[s]), kk * kBK, n0);
+        }
+      }
+      if (*abort) {
+        // Let the loads this thread may have started land before exiting.
+        for (int d = 0; d < T::kStages && it > 0; ++d) {
+          --it;
+          mbar_wait_drain(smem_u32(&bars->full[it % T::kStages]), (it / T::kStages) & 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(128, kBN, false, false);
+      uint32_t it = 0, tcount = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++tcount) {
+        const uint32_t buf = tcount % T::kBufs;
+        // The epilogue has drained this TMEM buffer's previous tile.
+        if (!mbar_wait(smem_u32(&bars->acc_empty[buf]), ((tcount / T::kBufs) & 1) ^ 1, abort,
+                       p.status, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + buf * T::kAccs * kBN;
+        for (int kk = 0; kk < ksteps; ++kk, ++it) {
+          const int s = static_cast<int>(it % T::kStages);
+          const uint32_t ph = (it / T::kStages) & 1;
+          if (!mbar_wait(smem_u32(&bars->full[s]), ph, abort, p.status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a = sA + s * T::kABytes, b = sB + s * kBBytes;
+#pragma unroll
+          for (int h = 0; h < T::kAccs; ++h) {
+#pragma unroll
+            for (int k4 = 0; k4 < kBK / 16; ++k4)
+              mma_bf16_ss(d + h * kBN, sdesc_sw128(a + h * 128 * 128 + k4 * 32, 16, 1024),
+                          sdesc_sw128(b + k4 * 32, 16, 1024), idesc, (kk > 0 || k4 > 0) ? 1u : 0u);
+          }
+          mma_commit(smem_u32(&bars->empty[s]));
+        }
+        if (!ok) break;
+        mma_commit(smem_u32(&bars->acc_full[buf]));
+      }
+      mma_commit(smem_u32(&bars->mma_drain));
+      mbar_wait_drain(smem_u32(&bars->mma_drain), 0);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    // Each warp drains 32 rows (its TMEM lane quarter) of one accumulator:
+    // all 256 columns with two accumulators, one 128-column half with one.
+    constexpr int kCols = T::kAccs * 128;
+    const int e = warp - 2;
+    const int quad = warp & 3;
+    const int h = T::kAccs == 2 ? (e >> 2) : 0;
+    const int col0 = T::kAccs == 2 ? 0 : (e >> 2) * 128;
+    const int row_in_tile = h * 128 + quad * 32 + lane;
+    uint32_t tcount = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++tcount) {
+      const uint32_t buf = tcount % T::kBufs;
+      if (!__all_sync(0xffffffffu, mbar_wait(smem_u32(&bars->acc_full[buf]),
+                                             (tcount / T::kBufs) & 1, abort, p.status,
+                                             kStatusTimeoutEpilogue)))
+        break;
+      tc_fence_after();
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(quad * 32) << 16) +
+                             (buf * T::kAccs + h) * kBN + col0;
+      const int m0 = (tile / p.tiles_n) * BM;
+      const int n0 = (tile % p.tiles_n) * kBN + col0;
+      uint32_t out[kCols / 2];
+#pragma unroll
+      for (int c = 0; c < kCols / 16; ++c) {
+        uint32_t r[16];
+        tmem_ld_wait_16(taddr + c * 16, r);
+#pragma unroll
+        for (int v = 0; v < 2; ++v) {
+          uint4 w = make_uint4(0u, 0u, 0u, 0u);
+          if (p.bias != nullptr)
+            w = __ldg(reinterpret_cast<const uint4*>(p.bias + n0 + c * 16 + v * 8));
+          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            out[c * 8 + v * 4 + i] =
+                pack_bf16x2(__uint_as_float(r[8 * v + 2 * i]) + __uint_as_float(wv[i] << 16),
+                            __uint_as_float(r[8 * v + 2 * i + 1]) +
+                                __uint_as_float(wv[i] & 0xffff0000u));
+        }
+      }
+      // The TMEM buffer is free for a later tile once every warp has read it.
+      tc_fence_before();
+      mbar_arrive(smem_u32(&bars->acc_empty[buf]));
+      const int row = m0 + row_in_tile;
+      if (row < p.m) {
+        uint4* dst = reinterpret_cast<uint4*>(p.c + static_cast<long long>(row) * p.ldc + n0);
+#pragma unroll
+        for (int v = 0; v < kCols / 8; ++v)
+          dst[v] = make_uint4(out[4 * v], out[4 * v + 1], out[4 * v + 2], out[4 * v + 3]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace lin
+}  // namespace erd
+
+using namespace erd;
+
+extern "C" int erd_linear_bf16(const void* x, int64_t ldx, const void* weight, int64_t ldw,
+                               const void* bias, void* y, int64_t ldy, int m, int n, int k,
+                               int* status, void* stream) {
+  using namespace erd::lin;
+  if (x == nullptr || weight == nullptr || y == nullptr) return kErrNullPointer;
+  if (m <= 0 || n <= 0 || k <= 0 || n % kBN != 0 || k % kBK != 0) return kErrBadShape;
+  if (ldx < k || ldw < k || ldy < n) return kErrBadShape;
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(y) || (bias != nullptr && !aligned16(bias)) ||
+      (ldx & 7) != 0 || (ldw & 7) != 0 || (ldy & 7) != 0)
+    return kErrMisaligned;
+  if (int rc = check_device_sm100()) return rc;
+
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  // Tile height: 256 rows unless 128-row tiles finish sooner on this many SMs
+  // (a 128-row tile costs about half of a 256-row one, plus 5 %).
+  const long long tiles_n = n / kBN;
+  const long long t256 = (m + 255) / 256 * tiles_n, t128 = (m + 127) / 128 * tiles_n;
+  const long long w256 = (t256 + sms - 1) / sms, w128 = (t128 + sms - 1) / sms;
+  const int bm = (w128 * 105 < w256 * 200) ? 128 : 256;
+  if (t128 > (1LL << 30)) return kErrTooLarge;
+
+  CUtensorMap ta, tb;
+  const int a_rows = m < bm ? m : bm;
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldx) * 2};
+    const uint32_t box[2] = {kBK, static_cast<uint32_t>(a_rows)};
+    if (encode_tensor_map(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims,
+                          strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return kErrTensorMap;
+  }
+  {
+    const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldw) * 2};
+    const uint32_t box[2] = {kBK, kBN};
+    if (encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(weight),
+                          dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+      return kErrTensorMap;
+  }
+  Params p;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.tiles_m = (m + bm - 1) / bm;
+  p.tiles_n = static_cast<int>(tiles_n);
+  p.a_rows = a_rows;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.c = static_cast<__nv_bfloat16*>(y);
+  p.ldc = ldy;
+  p.status = status;
+  const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
+  const unsigned grid = static_cast<unsigned>(tiles < sms ? tiles : sms);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (bm == 128) {
+    e = cudaFuncSetAttribute(linear_bf16_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Tile<128>::kSmemLaunchBytes);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    linear_bf16_kernel<128><<<grid, kThreads, Tile<128>::kSmemLaunchBytes, st>>>(ta, tb, p);
+  } else {
+    e = cudaFuncSetAttribute(linear_bf16_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Tile<256>::kSmemLaunchBytes);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    linear_bf16_kernel<256><<<grid, kThreads, Tile<256>::kSmemLaunchBytes, st>>>(ta, tb, p);
+  }
+  return static_cast<int>(cudaGetLastError());
+}

@@ -5,15 +5,15 @@ Follows ``EraserDiTAttentionProcessor.self_attn``
 across heads, 3D RoPE, attention with scale head_dim ** -0.5, flatten heads,
 output projection.  Data movement in HBM:
 
-1. one cuBLAS GEMM with the concatenated [Wq; Wk; Wv] writes Q|K|V
-   interleaved per token ([B, S, 6144] BF16);
+1. one GEMM (``erd_linear_bf16``, tcgen05) with the concatenated
+   [Wq; Wk; Wv] writes Q|K|V interleaved per token ([B, S, 6144] BF16);
 2. ``erd_qk_norm_rope`` normalises and rotates Q and K in place in that
    buffer (one read + one write of Q and K);
 3. ``erd_attn_fwd_bf16`` reads Q/K/V straight from the interleaved buffer via
    TMA (token stride 6144) and writes O in [B, S, H*D] order (or, with
    ``precision="fp8"``, ``erd_attn_fwd_fp8`` quantises them into its
    workspace first);
-4. one cuBLAS GEMM applies ``to_out[0]``.
+4. one GEMM (``erd_linear_bf16``) applies ``to_out[0]``.
 
 With a block-sparse plan (``sparse=``, see ``mask_sta.SparsePlan``) the layer
 runs on a sequence in the plan's tile order: the prologue takes each token's
@@ -24,9 +24,9 @@ step 3, and the output stays in tile order (every other step is per token).
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 from .attention import attention_bshd
+from .linear import linear_bf16
 from .mask_sta import sparse_attention_bshd
 from .operator_fusion import qk_norm_rope_into
 from .rotary import RopeAxisTable
@@ -83,7 +83,7 @@ class EraserDiTSelfAttention:
     def project_qkv(self, hidden_states: torch.Tensor) -> torch.Tensor:
         if self.qkv_fp8 is not None:
             return self.qkv_fp8.project(hidden_states)
-        return F.linear(hidden_states, self.w_qkv, self.b_qkv)
+        return linear_bf16(hidden_states, self.w_qkv, self.b_qkv)
 
     def core(self, qkv: torch.Tensor, rope, out: torch.Tensor | None = None,
              sparse=None) -> torch.Tensor:
@@ -110,7 +110,7 @@ class EraserDiTSelfAttention:
         return out
 
     def project_out(self, attn: torch.Tensor) -> torch.Tensor:
-        return F.linear(attn, self.w_out, self.b_out)
+        return linear_bf16(attn, self.w_out, self.b_out)
 
     def forward(self, hidden_states: torch.Tensor, rope: RopeAxisTable | tuple | None,
                 sparse=None) -> torch.Tensor:

@@ -7,7 +7,7 @@ wrapped around one EraserDiT self-attention layer
 floor-partitioned token range of the sequence (``mesh.py:163-169``) and all
 2048 channels of its tokens:
 
-1. QKV projection of the local tokens (cuBLAS);
+1. QKV projection of the local tokens (``erd_linear_bf16``);
 2. ``erd_qk_norm_rope`` normalises Q/K across all heads (the norm needs every
    head, so it runs before the exchange), applies 3D RoPE at the tokens'
    global grid positions, and writes Q/K/V straight into the send buffer,
@@ -24,7 +24,7 @@ floor-partitioned token range of the sequence (``mesh.py:163-169``) and all
    rank whose attention failed is reported by every peer (the protocol of
    ``layers/attention/sequence_parallel.py:257-300``) after all ranks have
    entered both collectives;
-6. heads are gathered back per token and ``to_out[0]`` is applied (cuBLAS).
+6. heads are gathered back per token and ``to_out[0]`` is applied (``erd_linear_bf16``).
 
 The two collectives are the only data-path communication; with CFG the
 Ulysses group is one branch's ranks (``eraserdit_b200.topology``).

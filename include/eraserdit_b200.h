@@ -306,6 +306,21 @@ int erd_peer_wait(const int32_t* flags, int n, int32_t epoch, int64_t timeout_ns
 int erd_quantize_e4m3(const void* x, void* out, int64_t n, float scale, void* stream);
 
 /*
+ * Linear layer y = x W^T + b with BF16 operands, FP32 accumulation, the bias
+ * added in FP32 and one rounding to BF16 (the semantics of torch's
+ * F.linear(x, W, b) for BF16 tensors): x [m, k] with row stride ldx, W [n, k]
+ * (nn.Linear's weight layout) with row stride ldw, bias [n] or NULL, y [m, n]
+ * with row stride ldy, strides in elements.  n must be a multiple of 256, k a
+ * multiple of 64; pointers and strides 16-byte aligned.
+ * Replaces the nn.Linear products of the self-attention path: the Q/K/V
+ * projections attn.to_q/to_k/to_v (models/dits/eraserdit_attention.py:248-253,
+ * run as one product over the concatenated weights) and the output projection
+ * to_out[0] (models/dits/eraserdit_attention.py:216-229).
+ */
+int erd_linear_bf16(const void* x, int64_t ldx, const void* weight, int64_t ldw, const void* bias,
+                    void* y, int64_t ldy, int m, int n, int k, int* status, void* stream);
+
+/*
  * SageAttention-style FP8 attention, head_dim 64: K smoothed by its per-head
  * token mean, Q and K quantised to E4M3 per 128-token block, V to E4M3 per
  * channel, P to E4M3 (scaled by 448), FP32 accumulation (tcgen05
