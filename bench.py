@@ -209,6 +209,17 @@ def cpu_sample_step(threads: int):
                         f"(batch, head) of fp32 SDPA over {SEQ} tokens")
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (as lscpu reports it)."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def cpu_baseline(steps: int = 12) -> dict:
     threads = os.cpu_count() or 1
     step, flop, sample = cpu_sample_step(threads)
@@ -218,6 +229,7 @@ def cpu_baseline(steps: int = 12) -> dict:
         step()
     dt = (time.perf_counter() - t0) / steps
     return {"value": flop / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "cpu_model": cpu_model(),
             "sample": sample + f"; {steps} timed steps of {dt:.2f} s"}
 
 
@@ -241,7 +253,7 @@ def run_reference(args, rank: int) -> None:
         "config": {"workload": WORKLOAD, "global_batch": BATCH, "seq_len": SEQ,
                    "parallelism": "cpu", "sample": sample},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "cpu_model": cpu_model(), "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 

@@ -15,14 +15,23 @@
 //   - shapes whose FP8 workspace exceeds ERD_FP8_STATIC_SCRATCH_BYTES (64 MiB)
 //     are rejected with kErrTooLarge before anything is enqueued;
 //   - the first call on each device looks the array's address up with
-//     cudaGetSymbolAddress (with that device current) and keeps it; make that
-//     first call before any stream capture;
+//     cudaGetSymbolAddress (with that device current) and keeps it together
+//     with the device's current context; make that first call before any
+//     stream capture.  A later call under a different context (the primary
+//     context was reset and re-created, e.g. after cudaDeviceReset) looks the
+//     address up again in that context;
+//   - the array is part of the library's CUDA module: each device holds its
+//     64 MiB from the moment the module is loaded there until the context
+//     ends (at the first kernel launch or symbol lookup of this library with
+//     lazy module loading, CUDA's default; at context creation with
+//     CUDA_MODULE_LOADING=EAGER), whether or not this entry point is called;
 //   - every call on a device uses the same array: calls that can overlap in
 //     time (on different streams, or from host threads without ordering
 //     between them) race on it;
 //   - nothing in the array has to start at zero: each call writes every byte
 //     it later reads (partial K sums and V maxima, the scales, the E4M3 tiles
 //     with their zero padding) before reading it.
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 #include <mutex>
@@ -40,7 +49,25 @@ constexpr int kMaxDevices = 64;
 constexpr int64_t kTileBytes = 3 * 128 * 64;  // Q, K and V^T bytes per 128-token tile
 
 std::mutex g_lookup;
-void* g_base[kMaxDevices];  // per device: 1024-aligned address inside g_fp8_scratch
+void* g_base[kMaxDevices];       // per device: 1024-aligned address inside g_fp8_scratch
+CUcontext g_ctx[kMaxDevices];    // the context g_base[device] was looked up in
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// cuCtxGetCurrent through the runtime's driver entry point (the library does
+// not link libcuda).
+CtxGetCurrentFn ctx_get_current() {
+  static CtxGetCurrentFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<CtxGetCurrentFn>(ptr);
+  });
+  return fn;
+}
 
 }  // namespace
 
@@ -53,14 +80,22 @@ int scratch_base(void** base) {
   cudaError_t e = cudaGetDevice(&device);
   if (e != cudaSuccess) return static_cast<int>(e);
   if (device < 0 || device >= kMaxDevices) return erd::kErrUnsupportedDevice;
+  CtxGetCurrentFn get_ctx = ctx_get_current();
+  if (get_ctx == nullptr) return erd::kErrUnsupportedDevice;
+  // No context may be current yet on this host thread (the runtime makes the
+  // primary context current lazily); the lookup below then makes it current.
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) ctx = nullptr;
   std::lock_guard<std::mutex> lock(g_lookup);
-  if (g_base[device] == nullptr) {
+  if (g_base[device] == nullptr || ctx == nullptr || g_ctx[device] != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_fp8_scratch);
     if (e != cudaSuccess) return static_cast<int>(e);
+    if (get_ctx(&ctx) != CUDA_SUCCESS || ctx == nullptr) return erd::kErrUnsupportedDevice;
     const uintptr_t a = (reinterpret_cast<uintptr_t>(p) + kWorkspaceAlign - 1) &
                         ~static_cast<uintptr_t>(kWorkspaceAlign - 1);
     g_base[device] = reinterpret_cast<void*>(a);
+    g_ctx[device] = ctx;
   }
   *base = g_base[device];
   return erd::kErrOk;

@@ -5,12 +5,15 @@
     python -m eraserdit_b200.profile_case fp8 --batch 1 --seq 16320 --iters 3
     python -m eraserdit_b200.profile_case sparse --batch 1 --heads 16 --iters 3
     python -m eraserdit_b200.profile_case ring --batch 1 --seq 16320 --iters 2
+    python -m eraserdit_b200.profile_case linear --batch 1 --seq 16320 --iters 3
 
 ``sparse`` runs the configuration-4 pattern (32640 tokens in tile order, the
 seeded ellipse mask) whatever ``--seq`` says.  ``ring`` attends ``--seq``
 queries to two ring pieces of ``--seq`` keys each with the carried state (the
 per-rank work of ring degree 2): per iteration, one launch writing the state
-and one reading it and writing the output.
+and one reading it and writing the output.  ``linear`` runs the QKV
+projection (``--batch`` x ``--seq`` rows of 2048 into 6144 columns, with bias)
+through ``erd_linear_bf16``.
 
 Each runs the named kernel ``iters`` times on seeded inputs (sized above L2 by
 default) and exits 0, so that an ncu capture (``-k``/``-c``) of one to three
@@ -26,7 +29,8 @@ import torch
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("kernel", choices=["attention", "prologue", "fp8", "sparse", "ring"])
+    ap.add_argument("kernel", choices=["attention", "prologue", "fp8", "sparse", "ring",
+                                       "linear"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seq", type=int, default=16320)
     ap.add_argument("--heads", type=int, default=32)
@@ -36,7 +40,15 @@ def main() -> None:
     torch.cuda.set_device(device)
     g = torch.Generator(device=device).manual_seed(0)
     from eraserdit_b200 import _native
-    if args.kernel == "ring":
+    if args.kernel == "linear":
+        from eraserdit_b200.linear import linear_bf16
+        x = torch.randn(args.batch * args.seq, 2048, generator=g, device=device).bfloat16()
+        w = (torch.randn(6144, 2048, generator=g, device=device) * 0.02).bfloat16()
+        b = torch.zeros(6144, device=device, dtype=torch.bfloat16)
+        y = torch.empty(args.batch * args.seq, 6144, device=device, dtype=torch.bfloat16)
+        for _ in range(args.iters):
+            linear_bf16(x, w, b, out=y)
+    elif args.kernel == "ring":
         from eraserdit_b200.ring import piece
         mk = lambda: torch.randn(args.batch, args.seq, args.heads, 64, generator=g,
                                  device=device).bfloat16()
