@@ -56,6 +56,8 @@ SIGNATURES = {
     "erd_quantize_e4m3": [_vp, _vp, _c_i64, _c_float, _vp],
     "erd_linear_bf16": [_vp, _c_i64, _vp, _c_i64, _vp, _vp, _c_i64, _c_int, _c_int, _c_int, _vp,
                         _vp],
+    "erd_linear_fp8": [_vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _c_i64, _c_int, _c_int, _c_int,
+                       _vp, _vp],
     "erd_attn_fwd_cross_bf16": [_vp, _vp, _vp] + [_c_i64] * 9 + [_c_int] * 4
                                + [_vp, _c_int, _c_float, _vp] + [_c_i64] * 3 + [_vp, _vp],
     "erd_ring_state_bytes": [_c_int, _c_int, _c_int, _c_int],

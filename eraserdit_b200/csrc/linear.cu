@@ -1,11 +1,14 @@
-// Linear layer y = x W^T + b on the sm_100a tensor cores: BF16 operands, FP32
-// accumulation in TMEM, bias added in FP32, BF16 output.
+// Linear layer y = x W^T + b on the sm_100a tensor cores: BF16 (or E4M3)
+// operands, FP32 accumulation in TMEM, bias added in FP32, BF16 output.
 //
 // Replaces the nn.Linear products of the reference's self-attention path:
 // the Q/K/V projections attn.to_q/to_k/to_v (models/dits/eraserdit_attention.py:
 // 248-253; nn.Linear(2048, 2048, bias=True), models/dits/eraserdit_transformer.py:
 // 253-263), run here as one product over the concatenated weights, and the
 // output projection to_out[0] (models/dits/eraserdit_attention.py:216-229).
+// The E4M3 instantiation (kind::f8f6f4, K = 32 per product, a per-column
+// scale in the epilogue) replaces the scaled_mm products of the FP8 shared
+// QKV projection (layers/quantization/qkv_fp8.py:29-63).
 //
 // Design: a persistent kernel, one CTA per SM, walking 256 x 256 (or, for
 // problems with few tiles, 128 x 256) output tiles row-block major, so the
@@ -49,8 +52,11 @@ __device__ __forceinline__ void tmem_ld_wait_16(uint32_t taddr, uint32_t (&r)[16
 }
 
 constexpr int kBN = 256;  // output columns per tile (one N=256 product)
-constexpr int kBK = 64;   // K per stage: one 128-byte swizzle atom of BF16
-constexpr int kBBytes = kBN * kBK * 2;  // 32 KB
+constexpr int kRowBytes = 128;  // K bytes per stage and row: one 128-byte swizzle atom
+// K elements per stage: 64 BF16 or 128 E4M3 (four K=16 or K=32 products either way).
+template <bool kFp8>
+constexpr int kBK = kFp8 ? 128 : 64;
+constexpr int kBBytes = kBN * kRowBytes;  // 32 KB
 constexpr int kEpilogueWarps = 8;
 constexpr int kThreads = 32 * (2 + kEpilogueWarps);
 
@@ -63,7 +69,7 @@ struct Tile {
   static constexpr int kAccs = BM / 128;     // M=128 accumulators per tile
   static constexpr int kBufs = 2 / kAccs;    // TMEM tile buffers
   static constexpr int kStages = BM == 128 ? 4 : 3;
-  static constexpr int kABytes = BM * kBK * 2;
+  static constexpr int kABytes = BM * kRowBytes;
   static constexpr int kSmemA = 0;
   static constexpr int kSmemB = kSmemA + kStages * kABytes;
   static constexpr int kSmemBar = kSmemB + kStages * kBBytes;
@@ -86,14 +92,15 @@ struct Params {
   int tiles_m, tiles_n;
   int a_rows;  // rows of the x tile box (BM, or m when m < BM)
   const __nv_bfloat16* bias;  // [n] or null
+  const float* col_scale;     // [n], E4M3 operands only: y = acc * col_scale + bias
   __nv_bfloat16* c;
   long long ldc;
   int* status;
 };
 
-template <int BM>
+template <int BM, bool kFp8>
 __global__ void __launch_bounds__(kThreads, 1)
-    linear_bf16_kernel(const __grid_constant__ CUtensorMap tmap_a,
+    linear_kernel(const __grid_constant__ CUtensorMap tmap_a,
                        const __grid_constant__ CUtensorMap tmap_b, const Params p) {
   using T = Tile<BM>;
   extern __shared__ uint8_t smem_raw[];
@@ -105,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int tiles = p.tiles_m * p.tiles_n;
-  const int ksteps = p.k / kBK;
+  const int ksteps = p.k / kBK<kFp8>;
   volatile int* abort = &bars->abort;
 
   if (threadIdx.x == 0) {
@@ -135,7 +142,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmap_a);
       tma_prefetch_desc(&tmap_b);
-      const uint32_t tx = static_cast<uint32_t>(p.a_rows * kBK * 2 + kBBytes);
+      const uint32_t tx = static_cast<uint32_t>(p.a_rows * kRowBytes + kBBytes);
       uint32_t it = 0;
       for (int tile = blockIdx.x; tile < tiles && !*abort; tile += gridDim.x) {
         const int m0 = (tile / p.tiles_n) * BM;
@@ -147,8 +154,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                          kStatusTimeoutProducer))
             break;
           mbar_arrive_expect_tx(smem_u32(&bars->full[s]), tx);
-          tma_load_2d(sA + s * T::kABytes, &tmap_a, smem_u32(&bars->full[s]), kk * kBK, m0);
-          tma_load_2d(sB + s * kBBytes, &tmap_b, smem_u32(&bars->full[s]), kk * kBK, n0);
+          tma_load_2d(sA + s * T::kABytes, &tmap_a, smem_u32(&bars->full[s]), kk * kBK<kFp8>,
+                      m0);
+          tma_load_2d(sB + s * kBBytes, &tmap_b, smem_u32(&bars->full[s]), kk * kBK<kFp8>, n0);
         }
       }
       if (*abort) {
@@ -162,7 +170,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(128, kBN, false, false);
+      constexpr uint32_t idesc =
+          kFp8 ? idesc_e4m3_f32(128, kBN) : idesc_bf16_f32(128, kBN, false, false);
       uint32_t it = 0, tcount = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++tcount) {
@@ -187,9 +196,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int h = 0; h < T::kAccs; ++h) {
 #pragma unroll
-            for (int k4 = 0; k4 < kBK / 16; ++k4)
-              mma_bf16_ss(d + h * kBN, sdesc_sw128(a + h * 128 * 128 + k4 * 32, 16, 1024),
-                          sdesc_sw128(b + k4 * 32, 16, 1024), idesc, (kk > 0 || k4 > 0) ? 1u : 0u);
+            for (int k4 = 0; k4 < 4; ++k4) {
+              // 32 bytes of K per product: 16 BF16 or 32 E4M3 values
+              const uint64_t da = sdesc_sw128(a + h * 128 * kRowBytes + k4 * 32, 16, 1024);
+              const uint64_t db = sdesc_sw128(b + k4 * 32, 16, 1024);
+              const uint32_t acc = (kk > 0 || k4 > 0) ? 1u : 0u;
+              if (kFp8)
+                mma_f8_ss(d + h * kBN, da, db, idesc, acc);
+              else
+                mma_bf16_ss(d + h * kBN, da, db, idesc, acc);
+            }
           }
           mma_commit(smem_u32(&bars->empty[s]));
         }
@@ -232,12 +248,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.bias != nullptr)
             w = __ldg(reinterpret_cast<const uint4*>(p.bias + n0 + c * 16 + v * 8));
           const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+          float a[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) a[i] = __uint_as_float(r[8 * v + i]);
+          if (kFp8) {
+            const float4* cs = reinterpret_cast<const float4*>(p.col_scale + n0 + c * 16 + v * 8);
+            const float4 c0 = __ldg(cs), c1 = __ldg(cs + 1);
+            a[0] *= c0.x; a[1] *= c0.y; a[2] *= c0.z; a[3] *= c0.w;
+            a[4] *= c1.x; a[5] *= c1.y; a[6] *= c1.z; a[7] *= c1.w;
+          }
 #pragma unroll
           for (int i = 0; i < 4; ++i)
-            out[c * 8 + v * 4 + i] =
-                pack_bf16x2(__uint_as_float(r[8 * v + 2 * i]) + __uint_as_float(wv[i] << 16),
-                            __uint_as_float(r[8 * v + 2 * i + 1]) +
-                                __uint_as_float(wv[i] & 0xffff0000u));
+            out[c * 8 + v * 4 + i] = pack_bf16x2(a[2 * i] + __uint_as_float(wv[i] << 16),
+                                                 a[2 * i + 1] + __uint_as_float(wv[i] & 0xffff0000u));
         }
       }
       // The TMEM buffer is free for a later tile once every warp has read it.
@@ -267,48 +290,57 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 using namespace erd;
 
-extern "C" int erd_linear_bf16(const void* x, int64_t ldx, const void* weight, int64_t ldw,
-                               const void* bias, void* y, int64_t ldy, int m, int n, int k,
-                               int* status, void* stream) {
+namespace {
+
+// Shared host path of the BF16 and E4M3 entry points: argument checks, tensor
+// maps, tile height and launch.
+template <bool kFp8>
+int linear_launch(const void* x, int64_t ldx, const void* weight, int64_t ldw,
+                  const float* col_scale, const void* bias, void* y, int64_t ldy, int m, int n,
+                  int k, int* status, void* stream) {
   using namespace erd::lin;
-  if (x == nullptr || weight == nullptr || y == nullptr) return kErrNullPointer;
-  if (m <= 0 || n <= 0 || k <= 0 || n % kBN != 0 || k % kBK != 0) return kErrBadShape;
+  constexpr int elem = kFp8 ? 1 : 2;  // bytes per operand element
+  if (x == nullptr || weight == nullptr || y == nullptr || (kFp8 && col_scale == nullptr))
+    return kErrNullPointer;
+  if (m <= 0 || n <= 0 || k <= 0 || n % kBN != 0 || k % kBK<kFp8> != 0) return kErrBadShape;
   if (ldx < k || ldw < k || ldy < n) return kErrBadShape;
-  if (!aligned16(x) || !aligned16(weight) || !aligned16(y) || (bias != nullptr && !aligned16(bias)) ||
-      (ldx & 7) != 0 || (ldw & 7) != 0 || (ldy & 7) != 0)
+  if (!aligned16(x) || !aligned16(weight) || !aligned16(y) ||
+      (bias != nullptr && !aligned16(bias)) || (col_scale != nullptr && !aligned16(col_scale)) ||
+      (ldx * elem) % 16 != 0 || (ldw * elem) % 16 != 0 || (ldy & 7) != 0)
     return kErrMisaligned;
   if (int rc = check_device_sm100()) return rc;
-
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return static_cast<int>(e);
   // Tile height: 256 rows unless 128-row tiles finish sooner on this many SMs.
-  // Measured on B200 at K = 2048: a wave of 128-row tiles takes 0.527 of a
-  // wave of 256-row ones, and a launch pays about 0.3 of a 256-row tile in
-  // pipeline fill and drain.
+  // Measured on B200 at K = 2048 (BF16): a wave of 128-row tiles takes 0.527
+  // of a wave of 256-row ones, and a launch pays about 0.3 of a 256-row tile
+  // in pipeline fill and drain.
   const long long tiles_n = n / kBN;
   const long long t256 = (m + 255) / 256 * tiles_n, t128 = (m + 127) / 128 * tiles_n;
   const long long w256 = (t256 + sms - 1) / sms, w128 = (t128 + sms - 1) / sms;
   const int bm = (w128 * 527 < w256 * 1000 + 300) ? 128 : 256;
   if (t128 > (1LL << 30)) return kErrTooLarge;
 
+  const CUtensorMapDataType dtype =
+      kFp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap ta, tb;
   const int a_rows = m < bm ? m : bm;
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(ldx) * 2};
-    const uint32_t box[2] = {kBK, static_cast<uint32_t>(a_rows)};
-    if (encode_tensor_map(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims,
-                          strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldx) * elem};
+    const uint32_t box[2] = {kBK<kFp8>, static_cast<uint32_t>(a_rows)};
+    if (encode_tensor_map(&ta, dtype, 2, const_cast<void*>(x), dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B))
       return kErrTensorMap;
   }
   {
     const uint64_t dims[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(ldw) * 2};
-    const uint32_t box[2] = {kBK, kBN};
-    if (encode_tensor_map(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(weight),
-                          dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
+    const uint64_t strides[1] = {static_cast<uint64_t>(ldw) * elem};
+    const uint32_t box[2] = {kBK<kFp8>, kBN};
+    if (encode_tensor_map(&tb, dtype, 2, const_cast<void*>(weight), dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B))
       return kErrTensorMap;
   }
   Params p;
@@ -319,6 +351,7 @@ extern "C" int erd_linear_bf16(const void* x, int64_t ldx, const void* weight, i
   p.tiles_n = static_cast<int>(tiles_n);
   p.a_rows = a_rows;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.col_scale = col_scale;
   p.c = static_cast<__nv_bfloat16*>(y);
   p.ldc = ldy;
   p.status = status;
@@ -326,15 +359,33 @@ extern "C" int erd_linear_bf16(const void* x, int64_t ldx, const void* weight, i
   const unsigned grid = static_cast<unsigned>(tiles < sms ? tiles : sms);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (bm == 128) {
-    e = cudaFuncSetAttribute(linear_bf16_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(linear_kernel<128, kFp8>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Tile<128>::kSmemLaunchBytes);
     if (e != cudaSuccess) return static_cast<int>(e);
-    linear_bf16_kernel<128><<<grid, kThreads, Tile<128>::kSmemLaunchBytes, st>>>(ta, tb, p);
+    linear_kernel<128, kFp8><<<grid, kThreads, Tile<128>::kSmemLaunchBytes, st>>>(ta, tb, p);
   } else {
-    e = cudaFuncSetAttribute(linear_bf16_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(linear_kernel<256, kFp8>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
                              Tile<256>::kSmemLaunchBytes);
     if (e != cudaSuccess) return static_cast<int>(e);
-    linear_bf16_kernel<256><<<grid, kThreads, Tile<256>::kSmemLaunchBytes, st>>>(ta, tb, p);
+    linear_kernel<256, kFp8><<<grid, kThreads, Tile<256>::kSmemLaunchBytes, st>>>(ta, tb, p);
   }
   return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+extern "C" int erd_linear_bf16(const void* x, int64_t ldx, const void* weight, int64_t ldw,
+                               const void* bias, void* y, int64_t ldy, int m, int n, int k,
+                               int* status, void* stream) {
+  return linear_launch<false>(x, ldx, weight, ldw, nullptr, bias, y, ldy, m, n, k, status,
+                              stream);
+}
+
+extern "C" int erd_linear_fp8(const void* x, int64_t ldx, const void* weight, int64_t ldw,
+                              const float* col_scale, const void* bias, void* y, int64_t ldy,
+                              int m, int n, int k, int* status, void* stream) {
+  return linear_launch<true>(x, ldx, weight, ldw, col_scale, bias, y, ldy, m, n, k, status,
+                             stream);
 }

@@ -5,10 +5,11 @@ one round-to-nearest E4M3 quantisation of the activations with a static,
 calibrated per-layer scale, and E4M3 weights with one scale per projection
 (amax / 448).  The reference runs three ``scaled_mm`` calls; here the three
 weights are concatenated into one [6144, 2048] E4M3 matrix with a per-column
-scale vector (each projection's scale over its 2048 columns), so that one
-cuBLASLt FP8 GEMM (``torch._scaled_mm``, row-wise scales, bias, BF16 out)
-writes the interleaved Q|K|V buffer the fused prologue reads.  The activation
-quantiser is ``erd_quantize_e4m3``.
+scale vector (the activation scale times each projection's weight scale over
+its 2048 columns), so that one tcgen05 E4M3 GEMM (``erd_linear_fp8``: FP32
+accumulation, scale and bias in the epilogue, BF16 out) writes the
+interleaved Q|K|V buffer the fused prologue reads.  The activation quantiser
+is ``erd_quantize_e4m3``.
 """
 
 from __future__ import annotations
@@ -80,13 +81,14 @@ class SharedQKV:
         self.weight = torch.cat(parts).contiguous()  # [6144, 2048] E4M3
         self.weight_scales = torch.stack(scales)      # per projection
         self.scale_b = self.weight_scales.repeat_interleave(2048).view(1, -1).contiguous()
+        # per output column: activation scale x the column's weight scale
+        self.col_scale = (self.scale_b.view(-1) * float(scale)).float().contiguous()
         zero = torch.zeros(2048, device=device)
         self.bias = torch.cat([zero if b is None else b.to(device).float() for b in (bq, bk, bv)]
                               ).to(torch.bfloat16).contiguous()
         self.activation_scale = float(scale)
         self.device = device
         self.calls = 0
-        self._scale_a: dict[int, torch.Tensor] = {}
 
     @classmethod
     def from_attention_module(cls, attn, scale: float, device) -> "SharedQKV":
@@ -96,15 +98,17 @@ class SharedQKV:
     def project(self, x: torch.Tensor) -> torch.Tensor:
         """[..., 2048] BF16 -> interleaved [..., 6144] BF16 (Q | K | V per token)."""
         rows = x.numel() // x.shape[-1]
-        if rows % 16:
-            raise ValueError("FP8 QKV needs a token count that is a multiple of 16")
         quant = quantize_activation(x.contiguous(), self.activation_scale).view(rows, 2048)
-        scale_a = self._scale_a.get(rows)
-        if scale_a is None:
-            scale_a = torch.full((rows, 1), self.activation_scale, device=self.device)
-            self._scale_a[rows] = scale_a
-        y = torch._scaled_mm(quant, self.weight.t(), scale_a=scale_a, scale_b=self.scale_b,
-                             bias=self.bias, out_dtype=torch.bfloat16, use_fast_accum=True)
+        y = torch.empty(rows, 6144, device=x.device, dtype=torch.bfloat16)
+        if rows:
+            lib = _native.load()
+            with torch.cuda.device(x.device):
+                rc = lib.erd_linear_fp8(quant.data_ptr(), 2048, self.weight.data_ptr(), 2048,
+                                        self.col_scale.data_ptr(), self.bias.data_ptr(),
+                                        y.data_ptr(), 6144, rows, 6144, 2048,
+                                        _native.status_word(x.device).data_ptr(),
+                                        _native.stream_handle(x.device))
+            _native.check(rc, "erd_linear_fp8")
         self.calls += 1
         return y.view(*x.shape[:-1], 6144)
 

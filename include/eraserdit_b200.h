@@ -321,6 +321,20 @@ int erd_linear_bf16(const void* x, int64_t ldx, const void* weight, int64_t ldw,
                     void* y, int64_t ldy, int m, int n, int k, int* status, void* stream);
 
 /*
+ * The same product with E4M3 operands (one byte each):
+ * y = BF16(acc * col_scale[j] + bias[j]) with acc the FP32 sum of x[i, :] *
+ * W[j, :]; col_scale [n] FP32 (activation scale times the weight scale of the
+ * column's projection), bias [n] BF16 or NULL.  n a multiple of 256, k a
+ * multiple of 128; strides in elements, rows 16-byte aligned.
+ * Replaces the scaled_mm products of SharedQKV (layers/quantization/qkv_fp8.py:
+ * 29-63: x_fp8 @ w_fp8^T with scale_a, scale_b, bias, BF16 out), as one
+ * product over the concatenated Q/K/V weights.
+ */
+int erd_linear_fp8(const void* x, int64_t ldx, const void* weight, int64_t ldw,
+                   const float* col_scale, const void* bias, void* y, int64_t ldy, int m, int n,
+                   int k, int* status, void* stream);
+
+/*
  * SageAttention-style FP8 attention, head_dim 64: K smoothed by its per-head
  * token mean, Q and K quantised to E4M3 per 128-token block, V to E4M3 per
  * channel, P to E4M3 (scaled by 448), FP32 accumulation (tcgen05

@@ -41,6 +41,18 @@ def test_shared_qkv_against_restatement():
     assert max_abs(got, want) <= 2e-2
     q, k, v = qkv(x.cuda())
     assert torch.equal(torch.cat([q, k, v], -1).cpu(), qkv.project(x.cuda()).cpu())
+    # and against torch's scaled_mm on the same E4M3 operands (the reference's
+    # product): both accumulate in fp32 and round once to BF16, so they differ
+    # by at most about one BF16 rounding of the result (plus summation order
+    # where the bias cancels the product)
+    from eraserdit_b200.qkv_fp8 import quantize_activation
+    xq = quantize_activation(x.cuda(), scale).view(-1, 2048)
+    lib = torch._scaled_mm(xq, qkv.weight.t(),
+                           scale_a=torch.full((xq.shape[0], 1), scale, device="cuda"),
+                           scale_b=qkv.scale_b, bias=qkv.bias, out_dtype=torch.bfloat16).float()
+    ours = qkv.project(x.cuda()).view(-1, 6144).float()
+    assert bool(((ours - lib).abs() <= lib.abs() * 2.0 ** -7 + 2e-3).all())
+    assert cosine(ours, lib) >= 0.99999
 
 
 def test_layer_with_fp8_qkv():
