@@ -144,6 +144,11 @@ class UlyssesSelfAttention:
         # A list here collects (start, end) CUDA events around every attention
         # launch on the stream it is enqueued on (for the benchmark's roofline).
         self.attention_events: list | None = None
+        # With the peer transport, a list here collects one dict per call of
+        # CUDA events at the phase boundaries (QKV GEMM, prologue + signal,
+        # wait for Q/K/V, attention + signal, wait for the rows, output GEMM).
+        self.phase_events: list | None = None
+        self._marks: dict | None = None
         if transport not in ("nccl", "peer"):
             raise ValueError("transport must be 'nccl' or 'peer'")
         if transport == "peer" and (head_chunks or 1) != 1:
@@ -401,6 +406,12 @@ class UlyssesSelfAttention:
                 bufs.close()
             self._peer = {}
 
+    def _mark(self, name: str) -> None:
+        if self._marks is not None:
+            event = torch.cuda.Event(enable_timing=True)
+            event.record()
+            self._marks[name] = event
+
     def peer_pre(self, x_local: torch.Tensor, rope, length: int):
         """QKV projection, then the prologue stores Q/K/V into the peers' recv1."""
         from .operator_fusion import qk_norm_rope_peer_into
@@ -418,6 +429,7 @@ class UlyssesSelfAttention:
             rope = rope.in_order(self.sparse.order)
         self._epoch += 1
         qkv = self.layer.project_qkv(x_local)
+        self._mark("qkv")
         q, k, v = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN], qkv[..., 2 * HIDDEN:]
         row1, qkv_gap = 3 * batch * hl * HEAD_DIM, batch * hl * HEAD_DIM
         # our slot in destination d's recv1[src = this rank][slot token][qkv][b][hl][d]
@@ -428,6 +440,7 @@ class UlyssesSelfAttention:
                                out_head_stride=HEAD_DIM, heads_per_dest=hl)
         stream = _native.stream_handle(x_local.device)
         signal(bufs, PHASE_IN, self.rank, n, self._epoch, stream)
+        self._mark("prologue")
         return bufs, lengths, batch
 
     def peer_attend(self, bufs, lengths, batch) -> bool:
@@ -440,6 +453,7 @@ class UlyssesSelfAttention:
         stream = _native.stream_handle(device)
         status = _native.status_word(device)
         wait(bufs, PHASE_IN, n, self._epoch, status, stream)
+        self._mark("wait_in")
         row1, qkv_gap = 3 * batch * hl * HEAD_DIM, batch * hl * HEAD_DIM
         base = bufs.local["recv1"]
         # this rank's heads of every owner's tokens: owner s's recv2[b][token][self.rank]
@@ -475,6 +489,7 @@ class UlyssesSelfAttention:
         self.calls += 1
         # every rank still signals, a failed one with the negative epoch
         signal(bufs, PHASE_OUT, self.rank, n, self._epoch if rc == 0 else -self._epoch, stream)
+        self._mark("attention")
         return rc == 0
 
     def peer_post(self, bufs, lengths, batch, ok: bool) -> torch.Tensor:
@@ -484,6 +499,7 @@ class UlyssesSelfAttention:
         device = bufs.device
         word = _native.status_word(device)
         wait(bufs, PHASE_OUT, n, self._epoch, word, _native.stream_handle(device))
+        self._mark("wait_out")
         if not ok:
             raise RuntimeError("local sequence-parallel attention failed")
         # status of this call: to pinned host memory now, inspected by drain()
@@ -501,9 +517,16 @@ class UlyssesSelfAttention:
 
     def _forward_peer(self, x_local: torch.Tensor, rope, length: int) -> torch.Tensor:
         self.drain()  # the previous call's status (normally complete by now)
+        self._marks = {} if self.phase_events is not None else None
+        self._mark("start")
         bufs, lengths, batch = self.peer_pre(x_local, rope, length)
         ok = self.peer_attend(bufs, lengths, batch)
-        return self.peer_post(bufs, lengths, batch, ok)
+        out = self.peer_post(bufs, lengths, batch, ok)
+        if self._marks is not None:
+            self._mark("out_proj")
+            self.phase_events.append(self._marks)
+            self._marks = None
+        return out
 
     # -------------------------------------------------------------- forward
     def forward(self, x_local: torch.Tensor, rope, length: int) -> torch.Tensor:
