@@ -17,6 +17,7 @@ def _rows(t):
 # (instruction-set paths); the fixtures were generated on one host, so the
 # table is compared to 1e-6 (|cos|, |sin| <= 1; on that host it is bit-exact).
 ROPE_ATOL = 1e-6
+BF16_HOST_ATOL = 4e-3
 
 
 def test_rope_table_matches_reference_class(golden):
@@ -56,7 +57,14 @@ def test_layer_bf16_matches_reference_processor(golden):
     cos, sin = ref.rope_table(c.batch, c.frames, c.height, c.width)
     with torch.no_grad():
         out = ref.self_attention_layer(x, p, cos, sin)
-    np.testing.assert_array_equal(_rows(out), golden["layer0_bf16_rows"])
+    got, want = _rows(out), golden["layer0_bf16_rows"]
+    # CPU BF16 GEMMs round differently on hosts with native BF16 dot products
+    # (AVX512-BF16/AMX) than on the host that made the fixtures, where this is
+    # bit-exact; across hosts the rows agree to a few BF16 steps of the
+    # output's scale (|out| <= 0.43 here, one step 2^-9).
+    np.testing.assert_allclose(got, want, rtol=0, atol=BF16_HOST_ATOL)
+    cos = float((got * want).sum() / np.sqrt((got * got).sum() * (want * want).sum()))
+    assert cos >= 0.99999
 
 
 @pytest.mark.parametrize("tag", ["a", "b"])
