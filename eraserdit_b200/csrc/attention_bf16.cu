@@ -53,10 +53,12 @@ constexpr int kTileBytes = kBlockM * kHeadDim * 2;  // 16 KB
 constexpr int kThreads = 320;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale only if max grows > 2^8
 // Of every 8 consecutive column pairs of a P row, this many are exponentiated
-// with the FMA-pipe polynomial and the rest with MUFU ex2, balancing the two
-// pipes (MUFU alone is the softmax bottleneck at head_dim 64).
+// with the FMA-pipe polynomial and the rest with MUFU ex2.  One in eight
+// measured 1-1.5 % faster than two in eight (and than all-MUFU) at
+// configuration 1: the polynomial costs about five more issue slots per pair
+// than MUFU, and issue slots are shared with the other softmax warpgroup.
 #ifndef ERD_POLY_EVERY8
-#define ERD_POLY_EVERY8 2
+#define ERD_POLY_EVERY8 1
 #endif
 constexpr int kPolyPairsPer8 = ERD_POLY_EVERY8;
 
