@@ -522,7 +522,10 @@ def run_single(args) -> None:
                 "h2d_bytes_per_step": host_x.numel() * host_x.element_size(),
                 "d2h_bytes_per_step": host_y[0].numel() * host_y[0].element_size(),
                 "copy_streams": 2},
-        "gpu_launches": ((4 if args.fp8 else 2) + (1 if args.qkv_fp8 else 0)) * args.steps,
+        # per layer step: QKV GEMM, prologue, attention (FP8: + statistics and
+        # quantisation passes), output GEMM; the FP8 QKV projection adds its
+        # activation quantiser
+        "gpu_launches": ((6 if args.fp8 else 4) + (1 if args.qkv_fp8 else 0)) * args.steps,
         "clocks": clock,
     }
     if plan is not None:

@@ -244,7 +244,11 @@ def run_sequence_parallel(args) -> None:
                         "h2d_bytes_per_step": x_local.numel() * x_local.element_size() * world,
                         "d2h_bytes_per_step": x_local.numel() * x_local.element_size() * world,
                         "copy_streams": 2},
-                "gpu_launches": (1 + (3 if args.fp8 else 1) * attn_launches) * args.steps,
+                # per step: QKV GEMM, prologue, the attention launches (FP8: three
+                # kernels each), output GEMM; the peer transport adds a signal and a
+                # bounded wait kernel around each of its two exchanges
+                "gpu_launches": ((7 if transport == "peer" else 3)
+                                 + (3 if args.fp8 else 1) * attn_launches) * args.steps,
                 "clocks": clock,
                 "parity": check,
             }
