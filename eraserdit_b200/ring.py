@@ -440,7 +440,7 @@ class UspSelfAttention(UlyssesSelfAttention):
     def forward(self, x_local: torch.Tensor, rope, length: int) -> torch.Tensor:
         """Layer output for this rank's tokens [B, L_rank, 2048]."""
         if self.transport == "peer":
-            self.drain()  # the previous call's status (normally complete by now)
+            self.drain(keep=max(self.status_lag, 1) - 1)  # earlier calls' status
             step = self.usp_peer_pre(x_local, rope, length)
             self.usp_peer_wait_in(step)
             ok = True
@@ -551,14 +551,7 @@ class UspSelfAttention(UlyssesSelfAttention):
         wait(bufs, PHASE_OUT, n, self._epoch, word, _native.stream_handle(device))
         if not ok:
             raise RuntimeError("local sequence-parallel attention failed")
-        if self._status_host is None:
-            self._status_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
-        host = self._status_host
-        host.copy_(word, non_blocking=True)
-        word.zero_()
-        event = torch.cuda.Event()
-        event.record()
-        self._pending = (event, host, bufs, self._epoch, n)
+        self._status_to_host(word, bufs, n)
         lme, lmax = step.lengths[self.rank], step.lmax
         heads = bufs.view("recv2", step.batch * lmax * n * hl * HEAD_DIM, torch.bfloat16)
         return self.layer.project_out(heads.view(step.batch, lmax, n * hl * HEAD_DIM)[:, :lme])

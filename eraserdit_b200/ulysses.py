@@ -63,6 +63,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from . import _native
+from .linear import linear_bf16
 from .layer import HEAD_DIM, HIDDEN, EraserDiTSelfAttention
 from .operator_fusion import qk_norm_rope_into
 from .rotary import RopeAxisTable
@@ -158,10 +159,17 @@ class UlyssesSelfAttention:
         self._peer: dict[tuple, object] = {}
         self._epoch = 0
         # Peer transport: a call's status word is copied to pinned host memory
-        # on the stream and inspected at the next call (or in drain()), so
-        # that no host synchronisation sits between consecutive layers.
-        self._pending = None
-        self._status_host = None
+        # on the stream and inspected ``status_lag`` calls later (or in
+        # drain()), so that no host synchronisation sits between consecutive
+        # layers: with the default lag of 2 the host enqueues call k + 1 while
+        # call k runs, and waits only for call k - 1 to have finished.
+        self.status_lag = 2
+        # Peer transport: token pieces per batch entry of the QKV projection,
+        # pipelined with the prologue's stores (None: select_qkv_chunks).
+        self.qkv_chunks: int | None = None
+        self._pro_stream = None
+        self._pending: list = []
+        self._status_pool: list = []
 
     def _bounds(self, length: int, rank: int) -> tuple[int, int]:
         if self.sparse is not None:
@@ -384,18 +392,31 @@ class UlyssesSelfAttention:
             self._peer[key] = bufs
         return bufs
 
-    def drain(self) -> None:
-        """Raise the error of the last peer-transport call, if it had one."""
-        pending, self._pending = self._pending, None
-        if pending is None:
-            return
-        event, host, bufs, epoch, n = pending
-        event.synchronize()
-        status = int(host[0])
-        if status:
-            flags = bufs.view("flags", 32, torch.int32)[16:16 + n].tolist()
-            bad = tuple(self.group_ranks[i] for i, f in enumerate(flags) if f != epoch)
-            raise SequenceParallelPeerError(bad or tuple(self.group_ranks))
+    def drain(self, keep: int = 0) -> None:
+        """Wait for the peer-transport calls still pending, all but the newest
+        ``keep``, oldest first, and raise the error of the first that failed."""
+        while len(self._pending) > keep:
+            event, host, bufs, epoch, n = self._pending.pop(0)
+            event.synchronize()
+            status = int(host[0])
+            self._status_pool.append(host)
+            if status:
+                # a later call may have moved the flags on: the ranks whose
+                # flag is not this call's epoch are named when it is still there
+                flags = bufs.view("flags", 32, torch.int32)[16:16 + n].tolist()
+                bad = tuple(self.group_ranks[i] for i, f in enumerate(flags) if f != epoch)
+                raise SequenceParallelPeerError(bad or tuple(self.group_ranks))
+
+    def _status_to_host(self, word: torch.Tensor, bufs, n: int) -> None:
+        """Copy this call's status word to pinned host memory on the stream,
+        clear it, and queue it for drain()."""
+        host = (self._status_pool.pop() if self._status_pool
+                else torch.empty(1, dtype=torch.int32, pin_memory=True))
+        host.copy_(word, non_blocking=True)
+        word.zero_()
+        event = torch.cuda.Event()
+        event.record()
+        self._pending.append((event, host, bufs, self._epoch, n))
 
     def close(self) -> None:
         """Release the peer buffers (after every rank's last call has finished)."""
@@ -411,6 +432,43 @@ class UlyssesSelfAttention:
             event = torch.cuda.Event(enable_timing=True)
             event.record()
             self._marks[name] = event
+
+    def _qkv_pieces(self, batch: int, tokens: int) -> list[tuple[int, int, int]]:
+        """(batch entry, first token, end token) pieces of the QKV projection
+        and prologue: ``qkv_chunks`` token ranges per batch entry."""
+        chunks = self.qkv_chunks if self.qkv_chunks is not None else select_qkv_chunks(
+            self.degree, tokens)
+        if chunks <= 1:
+            return [(0, 0, tokens)]
+        step = -(-tokens // chunks)
+        return [(b, t0, min(t0 + step, tokens)) for b in range(batch)
+                for t0 in range(0, tokens, step)]
+
+    def _pipelined_qkv(self, x_local: torch.Tensor, pieces, prologue) -> None:
+        """Project piece i on the current stream while the prologue of piece
+        i - 1 stores its rows over NVLink from a second stream: a prologue block
+        (64 registers, no shared memory) fits on an SM beside a GEMM CTA, so
+        the exchange overlaps the products instead of following them."""
+        device = x_local.device
+        current = torch.cuda.current_stream(device)
+        if self._pro_stream is None:
+            self._pro_stream = torch.cuda.Stream(device=device)
+        side = self._pro_stream
+        batch, tokens = x_local.shape[0], x_local.shape[1]
+        qkv = torch.empty(batch, tokens, 3 * HIDDEN, device=device, dtype=x_local.dtype)
+        side.wait_stream(current)  # the peers' slots are free (previous call's wait)
+        for b, t0, t1 in pieces:
+            part = qkv[b:b + 1, t0:t1]
+            linear_bf16(x_local[b:b + 1, t0:t1], self.layer.w_qkv, self.layer.b_qkv, out=part)
+            done = torch.cuda.Event()
+            done.record(current)
+            with torch.cuda.stream(side):
+                side.wait_event(done)
+                prologue(part, b, t0)
+        self._mark("qkv")
+        qkv.record_stream(side)
+        x_local.record_stream(side)
+        current.wait_stream(side)
 
     def peer_pre(self, x_local: torch.Tensor, rope, length: int):
         """QKV projection, then the prologue stores Q/K/V into the peers' recv1."""
@@ -428,16 +486,27 @@ class UlyssesSelfAttention:
                 and rope.grid_index is None):
             rope = rope.in_order(self.sparse.order)
         self._epoch += 1
-        qkv = self.layer.project_qkv(x_local)
-        self._mark("qkv")
-        q, k, v = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN], qkv[..., 2 * HIDDEN:]
         row1, qkv_gap = 3 * batch * hl * HEAD_DIM, batch * hl * HEAD_DIM
         # our slot in destination d's recv1[src = this rank][slot token][qkv][b][hl][d]
         dest = [bufs.peers["recv1"][d] + 2 * self.rank * lmax * row1 for d in range(n)]
-        qk_norm_rope_peer_into(q, k, v, self.layer.norm_q, self.layer.norm_k, self.layer.eps,
-                               rope, dest, qkv_gap, 2 * qkv_gap, token_offset=start,
-                               out_token_stride=row1, out_batch_stride=hl * HEAD_DIM,
-                               out_head_stride=HEAD_DIM, heads_per_dest=hl)
+
+        def prologue(qkv_part, b0: int, t0: int) -> None:
+            q, k, v = (qkv_part[..., :HIDDEN], qkv_part[..., HIDDEN:2 * HIDDEN],
+                       qkv_part[..., 2 * HIDDEN:])
+            off = 2 * (t0 * row1 + b0 * hl * HEAD_DIM)  # bytes into each destination slot
+            qk_norm_rope_peer_into(q, k, v, self.layer.norm_q, self.layer.norm_k,
+                                   self.layer.eps, rope, [d + off for d in dest], qkv_gap,
+                                   2 * qkv_gap, token_offset=start + t0,
+                                   out_token_stride=row1, out_batch_stride=hl * HEAD_DIM,
+                                   out_head_stride=HEAD_DIM, heads_per_dest=hl)
+
+        pieces = self._qkv_pieces(batch, end - start)
+        if len(pieces) == 1 or self.layer.qkv_fp8 is not None:
+            qkv = self.layer.project_qkv(x_local)
+            self._mark("qkv")
+            prologue(qkv, 0, 0)
+        else:
+            self._pipelined_qkv(x_local, pieces, prologue)
         stream = _native.stream_handle(x_local.device)
         signal(bufs, PHASE_IN, self.rank, n, self._epoch, stream)
         self._mark("prologue")
@@ -502,21 +571,13 @@ class UlyssesSelfAttention:
         self._mark("wait_out")
         if not ok:
             raise RuntimeError("local sequence-parallel attention failed")
-        # status of this call: to pinned host memory now, inspected by drain()
-        if getattr(self, "_status_host", None) is None:
-            self._status_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
-        host = self._status_host  # free again: drain() ran at the start of this call
-        host.copy_(word, non_blocking=True)
-        word.zero_()
-        event = torch.cuda.Event()
-        event.record()
-        self._pending = (event, host, bufs, self._epoch, n)
+        self._status_to_host(word, bufs, n)  # inspected by a later call's drain()
         lme, lmax = lengths[self.rank], max(lengths)
         heads = bufs.view("recv2", batch * lmax * n * hl * HEAD_DIM, torch.bfloat16)
         return self.layer.project_out(heads.view(batch, lmax, n * hl * HEAD_DIM)[:, :lme])
 
     def _forward_peer(self, x_local: torch.Tensor, rope, length: int) -> torch.Tensor:
-        self.drain()  # the previous call's status (normally complete by now)
+        self.drain(keep=max(self.status_lag, 1) - 1)  # earlier calls' status (complete by now)
         self._marks = {} if self.phase_events is not None else None
         self._mark("start")
         bufs, lengths, batch = self.peer_pre(x_local, rope, length)
@@ -592,6 +653,14 @@ class UlyssesSelfAttention:
     __call__ = forward
 
 
+def select_qkv_chunks(degree: int, tokens: int) -> int:
+    """Token pieces per batch entry of the peer transport's QKV projection and
+    prologue (the prologue of one piece overlaps the projection of the next).
+    One piece until measured otherwise."""
+    del degree, tokens
+    return 1
+
+
 def select_head_chunks(degree: int, length: int, local_heads: int, *, sparse: bool = False) -> int:
     """Head chunks of the overlap pipeline for one Ulysses layer call.
 
@@ -635,8 +704,8 @@ def emulate_attention_hook(layer: EraserDiTSelfAttention, degree: int, q: torch.
 
 
 def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, rope,
-                  sparse=None, head_chunks: int | None = None, transport: str = "nccl"
-                  ) -> list[torch.Tensor]:
+                  sparse=None, head_chunks: int | None = None, transport: str = "nccl",
+                  qkv_chunks: int | None = None) -> list[torch.Tensor]:
     """Run all ``degree`` ranks of the Ulysses layer inside one process on one
     device, exchanging chunks by copies (the same buffers and kernels as the
     NCCL path).  Returns each rank's output; used to check the data layout on
@@ -645,6 +714,8 @@ def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, r
     ranks = [UlyssesSelfAttention(layer, degree, r, exchange=None, sparse=sparse,
                                   head_chunks=head_chunks, transport=transport)
              for r in range(degree)]
+    for r in ranks:
+        r.qkv_chunks = qkv_chunks
     if transport == "peer":
         # every phase of every rank is enqueued before any rank waits on it
         bufs = [r.peer_buffers(x.shape[0], length, x.device, connect=False) for r in ranks]
