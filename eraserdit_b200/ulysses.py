@@ -63,7 +63,6 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from . import _native
-from .linear import linear_bf16
 from .layer import HEAD_DIM, HIDDEN, EraserDiTSelfAttention
 from .operator_fusion import qk_norm_rope_into
 from .rotary import RopeAxisTable
@@ -164,10 +163,6 @@ class UlyssesSelfAttention:
         # layers: with the default lag of 2 the host enqueues call k + 1 while
         # call k runs, and waits only for call k - 1 to have finished.
         self.status_lag = 2
-        # Peer transport: token pieces per batch entry of the QKV projection,
-        # pipelined with the prologue's stores (None: select_qkv_chunks).
-        self.qkv_chunks: int | None = None
-        self._pro_stream = None
         self._pending: list = []
         self._status_pool: list = []
 
@@ -433,43 +428,6 @@ class UlyssesSelfAttention:
             event.record()
             self._marks[name] = event
 
-    def _qkv_pieces(self, batch: int, tokens: int) -> list[tuple[int, int, int]]:
-        """(batch entry, first token, end token) pieces of the QKV projection
-        and prologue: ``qkv_chunks`` token ranges per batch entry."""
-        chunks = self.qkv_chunks if self.qkv_chunks is not None else select_qkv_chunks(
-            self.degree, tokens)
-        if chunks <= 1:
-            return [(0, 0, tokens)]
-        step = -(-tokens // chunks)
-        return [(b, t0, min(t0 + step, tokens)) for b in range(batch)
-                for t0 in range(0, tokens, step)]
-
-    def _pipelined_qkv(self, x_local: torch.Tensor, pieces, prologue) -> None:
-        """Project piece i on the current stream while the prologue of piece
-        i - 1 stores its rows over NVLink from a second stream: a prologue block
-        (64 registers, no shared memory) fits on an SM beside a GEMM CTA, so
-        the exchange overlaps the products instead of following them."""
-        device = x_local.device
-        current = torch.cuda.current_stream(device)
-        if self._pro_stream is None:
-            self._pro_stream = torch.cuda.Stream(device=device)
-        side = self._pro_stream
-        batch, tokens = x_local.shape[0], x_local.shape[1]
-        qkv = torch.empty(batch, tokens, 3 * HIDDEN, device=device, dtype=x_local.dtype)
-        side.wait_stream(current)  # the peers' slots are free (previous call's wait)
-        for b, t0, t1 in pieces:
-            part = qkv[b:b + 1, t0:t1]
-            linear_bf16(x_local[b:b + 1, t0:t1], self.layer.w_qkv, self.layer.b_qkv, out=part)
-            done = torch.cuda.Event()
-            done.record(current)
-            with torch.cuda.stream(side):
-                side.wait_event(done)
-                prologue(part, b, t0)
-        self._mark("qkv")
-        qkv.record_stream(side)
-        x_local.record_stream(side)
-        current.wait_stream(side)
-
     def peer_pre(self, x_local: torch.Tensor, rope, length: int):
         """QKV projection, then the prologue stores Q/K/V into the peers' recv1."""
         from .operator_fusion import qk_norm_rope_peer_into
@@ -486,27 +444,16 @@ class UlyssesSelfAttention:
                 and rope.grid_index is None):
             rope = rope.in_order(self.sparse.order)
         self._epoch += 1
+        qkv = self.layer.project_qkv(x_local)
+        self._mark("qkv")
+        q, k, v = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN], qkv[..., 2 * HIDDEN:]
         row1, qkv_gap = 3 * batch * hl * HEAD_DIM, batch * hl * HEAD_DIM
         # our slot in destination d's recv1[src = this rank][slot token][qkv][b][hl][d]
         dest = [bufs.peers["recv1"][d] + 2 * self.rank * lmax * row1 for d in range(n)]
-
-        def prologue(qkv_part, b0: int, t0: int) -> None:
-            q, k, v = (qkv_part[..., :HIDDEN], qkv_part[..., HIDDEN:2 * HIDDEN],
-                       qkv_part[..., 2 * HIDDEN:])
-            off = 2 * (t0 * row1 + b0 * hl * HEAD_DIM)  # bytes into each destination slot
-            qk_norm_rope_peer_into(q, k, v, self.layer.norm_q, self.layer.norm_k,
-                                   self.layer.eps, rope, [d + off for d in dest], qkv_gap,
-                                   2 * qkv_gap, token_offset=start + t0,
-                                   out_token_stride=row1, out_batch_stride=hl * HEAD_DIM,
-                                   out_head_stride=HEAD_DIM, heads_per_dest=hl)
-
-        pieces = self._qkv_pieces(batch, end - start)
-        if len(pieces) == 1 or self.layer.qkv_fp8 is not None:
-            qkv = self.layer.project_qkv(x_local)
-            self._mark("qkv")
-            prologue(qkv, 0, 0)
-        else:
-            self._pipelined_qkv(x_local, pieces, prologue)
+        qk_norm_rope_peer_into(q, k, v, self.layer.norm_q, self.layer.norm_k, self.layer.eps,
+                               rope, dest, qkv_gap, 2 * qkv_gap, token_offset=start,
+                               out_token_stride=row1, out_batch_stride=hl * HEAD_DIM,
+                               out_head_stride=HEAD_DIM, heads_per_dest=hl)
         stream = _native.stream_handle(x_local.device)
         signal(bufs, PHASE_IN, self.rank, n, self._epoch, stream)
         self._mark("prologue")
@@ -653,14 +600,6 @@ class UlyssesSelfAttention:
     __call__ = forward
 
 
-def select_qkv_chunks(degree: int, tokens: int) -> int:
-    """Token pieces per batch entry of the peer transport's QKV projection and
-    prologue (the prologue of one piece overlaps the projection of the next).
-    One piece until measured otherwise."""
-    del degree, tokens
-    return 1
-
-
 def select_head_chunks(degree: int, length: int, local_heads: int, *, sparse: bool = False) -> int:
     """Head chunks of the overlap pipeline for one Ulysses layer call.
 
@@ -704,8 +643,8 @@ def emulate_attention_hook(layer: EraserDiTSelfAttention, degree: int, q: torch.
 
 
 def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, rope,
-                  sparse=None, head_chunks: int | None = None, transport: str = "nccl",
-                  qkv_chunks: int | None = None) -> list[torch.Tensor]:
+                  sparse=None, head_chunks: int | None = None, transport: str = "nccl"
+                  ) -> list[torch.Tensor]:
     """Run all ``degree`` ranks of the Ulysses layer inside one process on one
     device, exchanging chunks by copies (the same buffers and kernels as the
     NCCL path).  Returns each rank's output; used to check the data layout on
@@ -714,8 +653,6 @@ def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, r
     ranks = [UlyssesSelfAttention(layer, degree, r, exchange=None, sparse=sparse,
                                   head_chunks=head_chunks, transport=transport)
              for r in range(degree)]
-    for r in ranks:
-        r.qkv_chunks = qkv_chunks
     if transport == "peer":
         # every phase of every rank is enqueued before any rank waits on it
         bufs = [r.peer_buffers(x.shape[0], length, x.device, connect=False) for r in ranks]

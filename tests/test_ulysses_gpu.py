@@ -72,20 +72,6 @@ def test_peer_transport_bitwise_equal_nccl_layout(degree, grid):
         assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("degree,grid,chunks", [(2, (2, 8, 12), 2), (4, (1, 7, 11), 3),
-                                                (8, (3, 5, 7), 2)])
-def test_peer_qkv_pieces_bitwise_equal_unpipelined(degree, grid, chunks):
-    """The QKV projection run in token pieces, each piece's prologue storing
-    over NVLink from a second stream while the next piece is projected, gives
-    every rank exactly the one-piece result."""
-    from eraserdit_b200.ulysses import emulate_ranks
-    layer, rope, x = _setup(*grid, 2, seed=20 + degree)
-    whole = emulate_ranks(layer, degree, x, rope, transport="peer", qkv_chunks=1)
-    pieces = emulate_ranks(layer, degree, x, rope, transport="peer", qkv_chunks=chunks)
-    for a, b in zip(whole, pieces):
-        assert torch.equal(a, b)
-
-
 def test_peer_wait_times_out_and_reports_failure():
     """Failure detection without a GPU fault: a wait on a flag that nothing
     sets ends after its limit with a status bit; a negative epoch (a failed
