@@ -19,7 +19,7 @@ from pathlib import Path
 import torch
 
 LIBRARY_PATH = Path(__file__).resolve().parent / "liberaserdit_b200.so"
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 _c_int, _c_i64, _c_float, _vp = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
@@ -56,6 +56,9 @@ SIGNATURES = {
     "erd_quantize_e4m3": [_vp, _vp, _c_i64, _c_float, _vp],
     "erd_linear_bf16": [_vp, _c_i64, _vp, _c_i64, _vp, _vp, _c_i64, _c_int, _c_int, _c_int, _vp,
                         _vp],
+    "erd_linear_bf16_scatter": [_vp, _c_i64, _vp, _c_i64, _vp, _vp, _c_i64, _c_int, _c_int,
+                                _c_int, _c_int, _vp, _c_int, _c_int, _c_int, _c_i64, _c_i64,
+                                _vp, _vp],
     "erd_linear_fp8": [_vp, _c_i64, _vp, _c_i64, _vp, _vp, _vp, _c_i64, _c_int, _c_int, _c_int,
                        _vp, _vp],
     "erd_attn_fwd_cross_bf16": [_vp, _vp, _vp] + [_c_i64] * 9 + [_c_int] * 4

@@ -96,6 +96,16 @@ struct Params {
   __nv_bfloat16* c;
   long long ldc;
   int* status;
+  // Columns from scatter_col0 on (a multiple of 256) go to other buffers
+  // instead of c: column j lands in scatter_base[g] with g = (j - scatter_col0)
+  // >> scatter_group_shift, at (row / scatter_rows) * scatter_bs + (row %
+  // scatter_rows) * scatter_ts + ((j - scatter_col0) & (group width - 1))
+  // elements.  scatter_col0 == n: nothing is scattered.
+  int scatter_col0;
+  int scatter_group_shift;
+  int scatter_rows;
+  long long scatter_bs, scatter_ts;
+  __nv_bfloat16* scatter_base[16];
 };
 
 template <int BM, bool kFp8>
@@ -267,11 +277,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(smem_u32(&bars->acc_empty[buf]));
       const int row = m0 + row_in_tile;
-      if (row < p.m) {
+      if (row < p.m && n0 < p.scatter_col0) {
         uint4* dst = reinterpret_cast<uint4*>(p.c + static_cast<long long>(row) * p.ldc + n0);
 #pragma unroll
         for (int v = 0; v < kCols / 8; ++v)
           dst[v] = make_uint4(out[4 * v], out[4 * v + 1], out[4 * v + 2], out[4 * v + 3]);
+      } else if (row < p.m) {
+        // Scattered columns (e.g. V straight into the peers' receive buffers).
+        const int b = row / p.scatter_rows;
+        const long long row_off =
+            b * p.scatter_bs + static_cast<long long>(row - b * p.scatter_rows) * p.scatter_ts;
+        const int mask = (1 << p.scatter_group_shift) - 1;
+#pragma unroll
+        for (int v = 0; v < kCols / 8; ++v) {
+          const int j = n0 + v * 8 - p.scatter_col0;
+          __nv_bfloat16* base = p.scatter_base[j >> p.scatter_group_shift];
+          *reinterpret_cast<uint4*>(base + row_off + (j & mask)) =
+              make_uint4(out[4 * v], out[4 * v + 1], out[4 * v + 2], out[4 * v + 3]);
+        }
       }
     }
   }
@@ -294,10 +317,17 @@ namespace {
 
 // Shared host path of the BF16 and E4M3 entry points: argument checks, tensor
 // maps, tile height and launch.
+struct Scatter {
+  int col0, group_shift, rows;
+  int64_t bs, ts;
+  void* const* bases;
+  int nbases;
+};
+
 template <bool kFp8>
 int linear_launch(const void* x, int64_t ldx, const void* weight, int64_t ldw,
                   const float* col_scale, const void* bias, void* y, int64_t ldy, int m, int n,
-                  int k, int* status, void* stream) {
+                  int k, int* status, void* stream, const Scatter* scatter = nullptr) {
   using namespace erd::lin;
   constexpr int elem = kFp8 ? 1 : 2;  // bytes per operand element
   if (x == nullptr || weight == nullptr || y == nullptr || (kFp8 && col_scale == nullptr))
@@ -355,6 +385,20 @@ int linear_launch(const void* x, int64_t ldx, const void* weight, int64_t ldw,
   p.c = static_cast<__nv_bfloat16*>(y);
   p.ldc = ldy;
   p.status = status;
+  p.scatter_col0 = n;
+  p.scatter_group_shift = 0;
+  p.scatter_rows = 1;
+  p.scatter_bs = p.scatter_ts = 0;
+  for (int g = 0; g < 16; ++g) p.scatter_base[g] = nullptr;
+  if (scatter != nullptr) {
+    p.scatter_col0 = scatter->col0;
+    p.scatter_group_shift = scatter->group_shift;
+    p.scatter_rows = scatter->rows;
+    p.scatter_bs = scatter->bs;
+    p.scatter_ts = scatter->ts;
+    for (int g = 0; g < scatter->nbases; ++g)
+      p.scatter_base[g] = static_cast<__nv_bfloat16*>(scatter->bases[g]);
+  }
   const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
   const unsigned grid = static_cast<unsigned>(tiles < sms ? tiles : sms);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -381,6 +425,34 @@ extern "C" int erd_linear_bf16(const void* x, int64_t ldx, const void* weight, i
                                int* status, void* stream) {
   return linear_launch<false>(x, ldx, weight, ldw, nullptr, bias, y, ldy, m, n, k, status,
                               stream);
+}
+
+extern "C" int erd_linear_bf16_scatter(const void* x, int64_t ldx, const void* weight,
+                                       int64_t ldw, const void* bias, void* y, int64_t ldy, int m,
+                                       int n, int k, int scatter_col0, void* const* dest_bases,
+                                       int ndest, int group_cols, int rows_per_batch,
+                                       int64_t dest_batch_stride, int64_t dest_token_stride,
+                                       int* status, void* stream) {
+  if (dest_bases == nullptr) return kErrNullPointer;
+  if (ndest <= 0 || ndest > 16 || group_cols < 128 || (group_cols & (group_cols - 1)) != 0 ||
+      scatter_col0 < 0 || scatter_col0 % erd::lin::kBN != 0 ||
+      static_cast<long long>(ndest) * group_cols != static_cast<long long>(n) - scatter_col0 ||
+      rows_per_batch <= 0 || m % rows_per_batch != 0 || dest_batch_stride < 0 ||
+      dest_token_stride < 0)
+    return kErrBadShape;
+  if (((dest_batch_stride | dest_token_stride) & 7) != 0) return kErrMisaligned;
+  for (int g = 0; g < ndest; ++g) {
+    if (dest_bases[g] == nullptr) return kErrNullPointer;
+    if (!aligned16(dest_bases[g])) return kErrMisaligned;
+  }
+  int shift = 0;
+  while ((1 << shift) < group_cols) ++shift;
+  const Scatter sc{scatter_col0, shift, rows_per_batch, dest_batch_stride, dest_token_stride,
+                   dest_bases, ndest};
+  // y is only written below scatter_col0; with nothing local it still passes
+  // the common checks (and is never dereferenced).
+  return linear_launch<false>(x, ldx, weight, ldw, nullptr, bias, y, ldy, m, n, k, status,
+                              stream, &sc);
 }
 
 extern "C" int erd_linear_fp8(const void* x, int64_t ldx, const void* weight, int64_t ldw,

@@ -83,3 +83,32 @@ def linear_bf16(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
     else:
         raise ValueError("x and out must be viewable as [rows, last dim] with one row stride")
     return out
+
+
+def linear_bf16_scatter(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
+                        out: torch.Tensor, scatter_col0: int, dest_bases: list[int],
+                        group_cols: int, batch_stride: int, token_stride: int) -> None:
+    """``linear_bf16`` of ``x`` [B, L, k] with the output columns from
+    ``scatter_col0`` on stored into ``dest_bases`` (``erd_linear_bf16_scatter``):
+    column j of token (b, t) goes to ``dest_bases[(j - scatter_col0) //
+    group_cols]`` at element ``b * batch_stride + t * token_stride +
+    (j - scatter_col0) % group_cols``; the columns below go to ``out`` [B, L, n]."""
+    import ctypes
+    if x.dim() != 3 or x.dtype != torch.bfloat16 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous BF16 [B, L, k] tensor")
+    n, k = weight.shape
+    if out.shape != (*x.shape[:-1], n) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous BF16 [B, L, n] tensor")
+    m = x.shape[0] * x.shape[1]
+    if m == 0:
+        return
+    lib = _native.load()
+    device = x.device
+    bases = (ctypes.c_void_p * len(dest_bases))(*dest_bases)
+    with torch.cuda.device(device):
+        rc = lib.erd_linear_bf16_scatter(
+            x.data_ptr(), k, weight.data_ptr(), weight.stride(0), _native.ptr(bias),
+            out.data_ptr(), n, m, n, k, scatter_col0, bases, len(dest_bases), group_cols,
+            x.shape[1], batch_stride, token_stride, _native.status_word(device).data_ptr(),
+            _native.stream_handle(device))
+    _native.check(rc, "erd_linear_bf16_scatter")

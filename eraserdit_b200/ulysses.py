@@ -64,6 +64,7 @@ import torch.nn.functional as F
 
 from . import _native
 from .layer import HEAD_DIM, HIDDEN, EraserDiTSelfAttention
+from .linear import linear_bf16_scatter
 from .operator_fusion import qk_norm_rope_into
 from .rotary import RopeAxisTable
 from .sequence_sharding import block_bounds, block_lengths, floor_bounds, floor_lengths
@@ -444,12 +445,23 @@ class UlyssesSelfAttention:
                 and rope.grid_index is None):
             rope = rope.in_order(self.sparse.order)
         self._epoch += 1
-        qkv = self.layer.project_qkv(x_local)
-        self._mark("qkv")
-        q, k, v = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN], qkv[..., 2 * HIDDEN:]
         row1, qkv_gap = 3 * batch * hl * HEAD_DIM, batch * hl * HEAD_DIM
         # our slot in destination d's recv1[src = this rank][slot token][qkv][b][hl][d]
         dest = [bufs.peers["recv1"][d] + 2 * self.rank * lmax * row1 for d in range(n)]
+        if self.layer.qkv_fp8 is None and x_local.is_contiguous():
+            # V needs no norm: the projection's epilogue stores it straight
+            # into the destinations' slots, and the prologue carries Q and K.
+            qkv = torch.empty(batch, end - start, 3 * HIDDEN, device=x_local.device,
+                              dtype=x_local.dtype)
+            linear_bf16_scatter(x_local, self.layer.w_qkv, self.layer.b_qkv, qkv, 2 * HIDDEN,
+                                [d + 2 * 2 * qkv_gap for d in dest], hl * HEAD_DIM,
+                                hl * HEAD_DIM, row1)
+            v = None
+        else:
+            qkv = self.layer.project_qkv(x_local)
+            v = qkv[..., 2 * HIDDEN:]
+        self._mark("qkv")
+        q, k = qkv[..., :HIDDEN], qkv[..., HIDDEN:2 * HIDDEN]
         qk_norm_rope_peer_into(q, k, v, self.layer.norm_q, self.layer.norm_k, self.layer.eps,
                                rope, dest, qkv_gap, 2 * qkv_gap, token_offset=start,
                                out_token_stride=row1, out_batch_stride=hl * HEAD_DIM,

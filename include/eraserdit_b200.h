@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define ERD_ABI_VERSION 4
+#define ERD_ABI_VERSION 5
 
 /* ABI version probe; replaces eraserdit_mask_sta_abi()
  * (layers/attention/backends/csrc/mask_sta/core.cu:767). */
@@ -319,6 +319,28 @@ int erd_quantize_e4m3(const void* x, void* out, int64_t n, float scale, void* st
  */
 int erd_linear_bf16(const void* x, int64_t ldx, const void* weight, int64_t ldw, const void* bias,
                     void* y, int64_t ldy, int m, int n, int k, int* status, void* stream);
+
+/*
+ * erd_linear_bf16 with the columns from scatter_col0 on stored into other
+ * buffers instead of y: column j >= scatter_col0 of row i goes to
+ * dest_bases[g], g = (j - scatter_col0) / group_cols, at element offset
+ * (i / rows_per_batch) * dest_batch_stride + (i % rows_per_batch) *
+ * dest_token_stride + (j - scatter_col0) % group_cols.  Columns below
+ * scatter_col0 go to y as in erd_linear_bf16.  scatter_col0 a multiple of 256,
+ * group_cols a power of two >= 128, ndest * group_cols == n - scatter_col0
+ * (at most 16 destinations), m a multiple of rows_per_batch, destinations and
+ * strides 16-byte aligned.
+ * On the Ulysses peer path this stores V (columns 4096..6143 of the
+ * concatenated projection) straight into every rank's receive slot over
+ * NVLink, in the layout of the seq->head all-to-all that follows the
+ * projection (layers/attention/qkv_packing.py:31-48, nccl_sequence.py:43-79):
+ * the projection's epilogue carries V's exchange, and the prologue only Q, K.
+ */
+int erd_linear_bf16_scatter(const void* x, int64_t ldx, const void* weight, int64_t ldw,
+                            const void* bias, void* y, int64_t ldy, int m, int n, int k,
+                            int scatter_col0, void* const* dest_bases, int ndest, int group_cols,
+                            int rows_per_batch, int64_t dest_batch_stride,
+                            int64_t dest_token_stride, int* status, void* stream);
 
 /*
  * The same product with E4M3 operands (one byte each):

@@ -76,3 +76,53 @@ def test_linear_rows_of_wider_slots():
     want = torch.stack([_fp32(x[i], w, b) for i in range(2)])
     assert y.shape == (2, 513, 2048)
     assert bool(((y.float() - want).abs() <= want.abs() * 2.0 ** -8 + 1e-3).all())
+
+
+@pytest.mark.parametrize("batch,tokens,n,col0,group", [(2, 4080, 6144, 4096, 256),
+                                                       (2, 300, 6144, 4096, 1024),
+                                                       (1, 517, 1024, 512, 128),
+                                                       (3, 129, 768, 0, 256)])
+def test_scatter_columns_equal_plain_product(batch, tokens, n, col0, group):
+    """erd_linear_bf16_scatter: the columns below col0 land in `out`, the rest in
+    the destination buffers at (b * batch_stride + t * token_stride + column
+    within the group), bit for bit what erd_linear_bf16 computes."""
+    from eraserdit_b200 import _native
+    from eraserdit_b200.linear import linear_bf16, linear_bf16_scatter
+    k = 2048
+    g = torch.Generator(device="cuda").manual_seed(batch * tokens + n)
+    x = torch.randn(batch, tokens, k, generator=g, device="cuda").bfloat16()
+    w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
+    bias = (torch.randn(n, generator=g, device="cuda") * 0.5).bfloat16()
+    want = linear_bf16(x, w, bias)
+    ndest = (n - col0) // group
+    batch_stride, token_stride = group + 64, batch * (group + 64) + 8
+    dests = [torch.full((tokens * token_stride + batch * batch_stride,), -7.0,
+                        device="cuda", dtype=torch.bfloat16) for _ in range(ndest)]
+    out = torch.zeros(batch, tokens, n, device="cuda", dtype=torch.bfloat16)
+    linear_bf16_scatter(x, w, bias, out, col0, [d.data_ptr() for d in dests], group,
+                        batch_stride, token_stride)
+    assert _native.read_status(x.device) == 0
+    assert torch.equal(out[..., :col0], want[..., :col0])
+    assert bool((out[..., col0:] == 0).all())  # scattered columns never touch out
+    for gi, d in enumerate(dests):
+        idx = (torch.arange(batch, device="cuda")[:, None, None] * batch_stride
+               + torch.arange(tokens, device="cuda")[None, :, None] * token_stride
+               + torch.arange(group, device="cuda")[None, None, :])
+        assert torch.equal(d[idx], want[..., col0 + gi * group:col0 + (gi + 1) * group])
+        hit = torch.zeros_like(d, dtype=torch.bool)
+        hit[idx.flatten()] = True
+        assert bool((d[~hit] == -7.0).all())  # nothing else written
+
+
+def test_scatter_rejects_bad_layouts():
+    from eraserdit_b200.linear import linear_bf16_scatter
+    x = torch.zeros(1, 8, 64, device="cuda", dtype=torch.bfloat16)
+    w = torch.zeros(512, 64, device="cuda", dtype=torch.bfloat16)
+    out = torch.zeros(1, 8, 512, device="cuda", dtype=torch.bfloat16)
+    d = torch.zeros(4096, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError):  # 3 x 128 columns do not cover n - col0 = 256
+        linear_bf16_scatter(x, w, None, out, 256, [d.data_ptr()] * 3, 128, 0, 256)
+    with pytest.raises(RuntimeError):  # group width not a power of two
+        linear_bf16_scatter(x, w, None, out, 256, [d.data_ptr()], 192, 0, 256)
+    with pytest.raises(RuntimeError):  # col0 not a multiple of 256
+        linear_bf16_scatter(x, w, None, out, 128, [d.data_ptr()] * 3, 128, 0, 256)
