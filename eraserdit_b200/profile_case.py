@@ -6,6 +6,7 @@
     python -m eraserdit_b200.profile_case sparse --batch 1 --heads 16 --iters 3
     python -m eraserdit_b200.profile_case ring --batch 1 --seq 16320 --iters 2
     python -m eraserdit_b200.profile_case linear --batch 1 --seq 16320 --iters 3
+    python -m eraserdit_b200.profile_case cudnn --batch 1 --seq 16320 --iters 3
 
 ``sparse`` runs the configuration-4 pattern (32640 tokens in tile order, the
 seeded ellipse mask) whatever ``--seq`` says.  ``ring`` attends ``--seq``
@@ -13,7 +14,9 @@ queries to two ring pieces of ``--seq`` keys each with the carried state (the
 per-rank work of ring degree 2): per iteration, one launch writing the state
 and one reading it and writing the output.  ``linear`` runs the QKV
 projection (``--batch`` x ``--seq`` rows of 2048 into 6144 columns, with bias)
-through ``erd_linear_bf16``.
+through ``erd_linear_bf16``.  ``cudnn`` runs torch's SDPA with the cuDNN backend
+on the same [B, H, S, 64] BF16 shape: a library yardstick for the attention
+kernel, not part of the path.
 
 Each runs the named kernel ``iters`` times on seeded inputs (sized above L2 by
 default) and exits 0, so that an ncu capture (``-k``/``-c``) of one to three
@@ -30,7 +33,7 @@ import torch
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("kernel", choices=["attention", "prologue", "fp8", "sparse", "ring",
-                                       "linear"])
+                                       "linear", "cudnn"])
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seq", type=int, default=16320)
     ap.add_argument("--heads", type=int, default=32)
@@ -40,6 +43,15 @@ def main() -> None:
     torch.cuda.set_device(device)
     g = torch.Generator(device=device).manual_seed(0)
     from eraserdit_b200 import _native
+    if args.kernel == "cudnn":
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        q, k, v = (torch.randn(args.batch, args.heads, args.seq, 64, generator=g,
+                               device=device).bfloat16() for _ in range(3))
+        with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+            for _ in range(args.iters):
+                torch.nn.functional.scaled_dot_product_attention(q, k, v, scale=0.125)
+        torch.cuda.synchronize()
+        return
     if args.kernel == "linear":
         from eraserdit_b200.linear import linear_bf16
         x = torch.randn(args.batch * args.seq, 2048, generator=g, device=device).bfloat16()
