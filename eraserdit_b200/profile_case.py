@@ -13,7 +13,8 @@ seeded ellipse mask) whatever ``--seq`` says.  ``ring`` attends ``--seq``
 queries to two ring pieces of ``--seq`` keys each with the carried state (the
 per-rank work of ring degree 2): per iteration, one launch writing the state
 and one reading it and writing the output.  ``linear`` runs the QKV
-projection (``--batch`` x ``--seq`` rows of 2048 into 6144 columns, with bias)
+projection (``--batch`` x ``--seq`` rows of 2048 into ``--n`` columns, 6144 by
+default, with bias)
 through ``erd_linear_bf16``.  ``cudnn`` runs torch's SDPA with the cuDNN backend
 on the same [B, H, S, 64] BF16 shape: a library yardstick for the attention
 kernel, not part of the path.
@@ -37,6 +38,7 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--seq", type=int, default=16320)
     ap.add_argument("--heads", type=int, default=32)
+    ap.add_argument("--n", type=int, default=6144, help="linear: output columns")
     ap.add_argument("--iters", type=int, default=3)
     args = ap.parse_args()
     device = torch.device("cuda", 0)
@@ -55,9 +57,9 @@ def main() -> None:
     if args.kernel == "linear":
         from eraserdit_b200.linear import linear_bf16
         x = torch.randn(args.batch * args.seq, 2048, generator=g, device=device).bfloat16()
-        w = (torch.randn(6144, 2048, generator=g, device=device) * 0.02).bfloat16()
-        b = torch.zeros(6144, device=device, dtype=torch.bfloat16)
-        y = torch.empty(args.batch * args.seq, 6144, device=device, dtype=torch.bfloat16)
+        w = (torch.randn(args.n, 2048, generator=g, device=device) * 0.02).bfloat16()
+        b = torch.zeros(args.n, device=device, dtype=torch.bfloat16)
+        y = torch.empty(args.batch * args.seq, args.n, device=device, dtype=torch.bfloat16)
         for _ in range(args.iters):
             linear_bf16(x, w, b, out=y)
     elif args.kernel == "ring":
