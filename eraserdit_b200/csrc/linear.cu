@@ -73,7 +73,11 @@ struct Tile {
   static constexpr int kSmemA = 0;
   static constexpr int kSmemB = kSmemA + kStages * kABytes;
   static constexpr int kSmemBar = kSmemB + kStages * kBBytes;
-  static constexpr int kSmemLaunchBytes = kSmemBar + 1024 + 1024;  // + base alignment
+  // Per epilogue warp, a 32-row x 64-column staging block (4 KB) for the
+  // scattered columns, so that their stores leave as 128-byte row pieces.
+  static constexpr int kSmemStage = kSmemBar + 1024;
+  static constexpr int kStageBytes = 32 * 64 * 2;
+  static constexpr int kSmemLaunchBytes = kSmemStage + 8 * kStageBytes + 1024;  // + base alignment
   static_assert(kSmemLaunchBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -108,7 +112,7 @@ struct Params {
   __nv_bfloat16* scatter_base[16];
 };
 
-template <int BM, bool kFp8>
+template <int BM, bool kFp8, bool kScatter>
 __global__ void __launch_bounds__(kThreads, 1)
     linear_kernel(const __grid_constant__ CUtensorMap tmap_a,
                        const __grid_constant__ CUtensorMap tmap_b, const Params p) {
@@ -277,23 +281,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(smem_u32(&bars->acc_empty[buf]));
       const int row = m0 + row_in_tile;
-      if (row < p.m && n0 < p.scatter_col0) {
-        uint4* dst = reinterpret_cast<uint4*>(p.c + static_cast<long long>(row) * p.ldc + n0);
+      if (!kScatter || n0 < p.scatter_col0) {
+        if (row < p.m) {
+          uint4* dst =
+              reinterpret_cast<uint4*>(p.c + static_cast<long long>(row) * p.ldc + n0);
 #pragma unroll
-        for (int v = 0; v < kCols / 8; ++v)
-          dst[v] = make_uint4(out[4 * v], out[4 * v + 1], out[4 * v + 2], out[4 * v + 3]);
-      } else if (row < p.m) {
-        // Scattered columns (e.g. V straight into the peers' receive buffers).
+          for (int v = 0; v < kCols / 8; ++v)
+            dst[v] = make_uint4(out[4 * v], out[4 * v + 1], out[4 * v + 2], out[4 * v + 3]);
+        }
+      } else {
+        // Scattered columns (e.g. V straight into the peers' receive buffers,
+        // over NVLink): 64 columns at a time go through this warp's staging
+        // block, so that each store instruction writes four 128-byte row
+        // pieces instead of 32 separate 16-byte ones.
         const int b = row / p.scatter_rows;
-        const long long row_off =
+        const long long my_off =
             b * p.scatter_bs + static_cast<long long>(row - b * p.scatter_rows) * p.scatter_ts;
         const int mask = (1 << p.scatter_group_shift) - 1;
+        uint8_t* stage = smem + T::kSmemStage + e * T::kStageBytes;
+        const int sub = lane >> 3, chunk = lane & 7;  // row within a group of 4, 16-byte chunk
 #pragma unroll
-        for (int v = 0; v < kCols / 8; ++v) {
-          const int j = n0 + v * 8 - p.scatter_col0;
-          __nv_bfloat16* base = p.scatter_base[j >> p.scatter_group_shift];
-          *reinterpret_cast<uint4*>(base + row_off + (j & mask)) =
-              make_uint4(out[4 * v], out[4 * v + 1], out[4 * v + 2], out[4 * v + 3]);
+        for (int piece = 0; piece < kCols / 64; ++piece) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const int v = piece * 8 + c;
+            *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) * 16)) =
+                make_uint4(out[4 * v], out[4 * v + 1], out[4 * v + 2], out[4 * v + 3]);
+          }
+          __syncwarp();
+          const int j = n0 + piece * 64 + chunk * 8 - p.scatter_col0;
+          __nv_bfloat16* base = p.scatter_base[j >> p.scatter_group_shift] + (j & mask);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int rr = 4 * q + sub;  // staged row (the lane that drained it)
+            const long long off = __shfl_sync(0xffffffffu, my_off, rr);
+            const bool valid = __shfl_sync(0xffffffffu, row < p.m ? 1 : 0, rr) != 0;
+            const uint4 val =
+                *reinterpret_cast<const uint4*>(stage + rr * 128 + ((chunk ^ (rr & 7)) * 16));
+            if (valid) *reinterpret_cast<uint4*>(base + off) = val;
+          }
+          __syncwarp();
         }
       }
     }
@@ -317,6 +344,18 @@ namespace {
 
 // Shared host path of the BF16 and E4M3 entry points: argument checks, tensor
 // maps, tile height and launch.
+template <int BM, bool kFp8, bool kScatter>
+cudaError_t launch_linear(unsigned grid, cudaStream_t st, const CUtensorMap& ta,
+                          const CUtensorMap& tb, const lin::Params& p) {
+  using namespace erd::lin;
+  cudaError_t e = cudaFuncSetAttribute(linear_kernel<BM, kFp8, kScatter>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       Tile<BM>::kSmemLaunchBytes);
+  if (e != cudaSuccess) return e;
+  linear_kernel<BM, kFp8, kScatter><<<grid, kThreads, Tile<BM>::kSmemLaunchBytes, st>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
 struct Scatter {
   int col0, group_shift, rows;
   int64_t bs, ts;
@@ -403,18 +442,13 @@ int linear_launch(const void* x, int64_t ldx, const void* weight, int64_t ldw,
   const unsigned grid = static_cast<unsigned>(tiles < sms ? tiles : sms);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (bm == 128) {
-    e = cudaFuncSetAttribute(linear_kernel<128, kFp8>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Tile<128>::kSmemLaunchBytes);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    linear_kernel<128, kFp8><<<grid, kThreads, Tile<128>::kSmemLaunchBytes, st>>>(ta, tb, p);
+    e = scatter != nullptr ? launch_linear<128, kFp8, true>(grid, st, ta, tb, p)
+                           : launch_linear<128, kFp8, false>(grid, st, ta, tb, p);
   } else {
-    e = cudaFuncSetAttribute(linear_kernel<256, kFp8>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Tile<256>::kSmemLaunchBytes);
-    if (e != cudaSuccess) return static_cast<int>(e);
-    linear_kernel<256, kFp8><<<grid, kThreads, Tile<256>::kSmemLaunchBytes, st>>>(ta, tb, p);
+    e = scatter != nullptr ? launch_linear<256, kFp8, true>(grid, st, ta, tb, p)
+                           : launch_linear<256, kFp8, false>(grid, st, ta, tb, p);
   }
+  if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -164,6 +164,9 @@ class UlyssesSelfAttention:
         # layers: with the default lag of 2 the host enqueues call k + 1 while
         # call k runs, and waits only for call k - 1 to have finished.
         self.status_lag = 2
+        # Peer transport: store V from the QKV projection's epilogue (None:
+        # use_v_scatter's measured policy).
+        self.v_scatter: bool | None = None
         self._pending: list = []
         self._status_pool: list = []
 
@@ -448,7 +451,8 @@ class UlyssesSelfAttention:
         row1, qkv_gap = 3 * batch * hl * HEAD_DIM, batch * hl * HEAD_DIM
         # our slot in destination d's recv1[src = this rank][slot token][qkv][b][hl][d]
         dest = [bufs.peers["recv1"][d] + 2 * self.rank * lmax * row1 for d in range(n)]
-        if self.layer.qkv_fp8 is None and x_local.is_contiguous():
+        if (self.v_scatter if self.v_scatter is not None else use_v_scatter(n)) and (
+                self.layer.qkv_fp8 is None and x_local.is_contiguous()):
             # V needs no norm: the projection's epilogue stores it straight
             # into the destinations' slots, and the prologue carries Q and K.
             qkv = torch.empty(batch, end - start, 3 * HIDDEN, device=x_local.device,
@@ -612,6 +616,16 @@ class UlyssesSelfAttention:
     __call__ = forward
 
 
+def use_v_scatter(degree: int) -> bool:
+    """Whether the peer transport's QKV projection stores V into the peers'
+    slots from its epilogue (``erd_linear_bf16_scatter``) instead of the
+    prologue copying it.  Measured with 16-byte per-row remote stores: QKV GEMM +
+    prologue 0.902 -> 0.852 ms on 2 GPUs, but 0.318 -> 0.376 ms on 8, where each
+    rank's short GEMM meets seven destinations; the epilogue now writes 128-byte
+    row pieces, and the policy stays at the measured gain (2 ranks)."""
+    return degree <= 2
+
+
 def select_head_chunks(degree: int, length: int, local_heads: int, *, sparse: bool = False) -> int:
     """Head chunks of the overlap pipeline for one Ulysses layer call.
 
@@ -655,8 +669,8 @@ def emulate_attention_hook(layer: EraserDiTSelfAttention, degree: int, q: torch.
 
 
 def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, rope,
-                  sparse=None, head_chunks: int | None = None, transport: str = "nccl"
-                  ) -> list[torch.Tensor]:
+                  sparse=None, head_chunks: int | None = None, transport: str = "nccl",
+                  v_scatter: bool | None = None) -> list[torch.Tensor]:
     """Run all ``degree`` ranks of the Ulysses layer inside one process on one
     device, exchanging chunks by copies (the same buffers and kernels as the
     NCCL path).  Returns each rank's output; used to check the data layout on
@@ -665,6 +679,8 @@ def emulate_ranks(layer: EraserDiTSelfAttention, degree: int, x: torch.Tensor, r
     ranks = [UlyssesSelfAttention(layer, degree, r, exchange=None, sparse=sparse,
                                   head_chunks=head_chunks, transport=transport)
              for r in range(degree)]
+    for r in ranks:
+        r.v_scatter = v_scatter
     if transport == "peer":
         # every phase of every rank is enqueued before any rank waits on it
         bufs = [r.peer_buffers(x.shape[0], length, x.device, connect=False) for r in ranks]

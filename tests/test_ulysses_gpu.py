@@ -72,6 +72,18 @@ def test_peer_transport_bitwise_equal_nccl_layout(degree, grid):
         assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("degree,grid", [(2, (1, 7, 11)), (4, (2, 8, 12)), (8, (3, 5, 7))])
+def test_peer_v_from_projection_epilogue_bitwise_equal(degree, grid):
+    """V stored into the peers' slots by the QKV projection's epilogue
+    (erd_linear_bf16_scatter) or copied by the prologue: the same result."""
+    from eraserdit_b200.ulysses import emulate_ranks
+    layer, rope, x = _setup(*grid, 2, seed=30 + degree)
+    copied = emulate_ranks(layer, degree, x, rope, transport="peer", v_scatter=False)
+    scattered = emulate_ranks(layer, degree, x, rope, transport="peer", v_scatter=True)
+    for a, b in zip(copied, scattered):
+        assert torch.equal(a, b)
+
+
 def test_peer_wait_times_out_and_reports_failure():
     """Failure detection without a GPU fault: a wait on a flag that nothing
     sets ends after its limit with a status bit; a negative epoch (a failed
