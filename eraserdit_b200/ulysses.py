@@ -618,12 +618,13 @@ class UlyssesSelfAttention:
 
 def use_v_scatter(degree: int) -> bool:
     """Whether the peer transport's QKV projection stores V into the peers'
-    slots from its epilogue (``erd_linear_bf16_scatter``) instead of the
-    prologue copying it.  Measured with 16-byte per-row remote stores: QKV GEMM +
-    prologue 0.902 -> 0.852 ms on 2 GPUs, but 0.318 -> 0.376 ms on 8, where each
-    rank's short GEMM meets seven destinations; the epilogue now writes 128-byte
-    row pieces, and the policy stays at the measured gain (2 ranks)."""
-    return degree <= 2
+    slots from its epilogue (``erd_linear_bf16_scatter``, 128-byte row pieces
+    staged through shared memory) instead of the prologue copying it.
+    Measured per layer (QKV GEMM + prologue, same box, with / without): 2 ranks
+    0.830 / 0.903 ms, 8 ranks 0.286-0.295 / 0.317-0.322 ms (3.434 / 3.465 ms a
+    layer)."""
+    del degree
+    return True
 
 
 def select_head_chunks(degree: int, length: int, local_heads: int, *, sparse: bool = False) -> int:
