@@ -441,12 +441,16 @@ int linear_launch(const void* x, int64_t ldx, const void* weight, int64_t ldw,
   const long long tiles = static_cast<long long>(p.tiles_m) * p.tiles_n;
   const unsigned grid = static_cast<unsigned>(tiles < sms ? tiles : sms);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (bm == 128) {
-    e = scatter != nullptr ? launch_linear<128, kFp8, true>(grid, st, ta, tb, p)
-                           : launch_linear<128, kFp8, false>(grid, st, ta, tb, p);
+  if (scatter != nullptr) {
+    if constexpr (kFp8) {
+      return kErrBadShape;  // the scattered epilogue serves the BF16 product only
+    } else {
+      e = bm == 128 ? launch_linear<128, false, true>(grid, st, ta, tb, p)
+                    : launch_linear<256, false, true>(grid, st, ta, tb, p);
+    }
   } else {
-    e = scatter != nullptr ? launch_linear<256, kFp8, true>(grid, st, ta, tb, p)
-                           : launch_linear<256, kFp8, false>(grid, st, ta, tb, p);
+    e = bm == 128 ? launch_linear<128, kFp8, false>(grid, st, ta, tb, p)
+                  : launch_linear<256, kFp8, false>(grid, st, ta, tb, p);
   }
   if (e != cudaSuccess) return static_cast<int>(e);
   return static_cast<int>(cudaGetLastError());
