@@ -77,7 +77,9 @@ def profiled_traffic(kernel: str) -> float | None:
 class ClockSampler:
     """SM clock and clock-event (throttle) reasons sampled during the timed region.
 
-    Reads NVML from a thread every 5 ms (read-only queries); falls back to
+    Reads NVML from a thread every ``interval`` seconds (read-only queries:
+    5 ms on one GPU, 20 ms per rank on several, where eight processes polling
+    the driver would otherwise share it with the short layer steps); falls back to
     ``nvidia-smi -lms 50`` when NVML is unavailable.  Nothing is changed on the
     device."""
 
@@ -156,7 +158,8 @@ class ClockSampler:
                               for bit, name in self.REASONS.items() if bits & bit})
             return {"sm_mhz": statistics.median(sm) if sm else None,
                     "sm_max_mhz": float(self.max_sm) if self.max_sm else None,
-                    "reasons": reasons, "samples": len(sm), "source": "nvml 5 ms"}
+                    "reasons": reasons, "samples": len(sm),
+                    "source": f"nvml {self.interval * 1e3:.0f} ms"}
         if self.proc is None or self.file is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         self.file.flush()

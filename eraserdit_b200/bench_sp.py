@@ -173,7 +173,7 @@ def run_sequence_parallel(args) -> None:
         check = _check_against_single(B, y_local, branch, tokens, references, rank)
         del y_local, references
 
-        clocks = B.ClockSampler(local)
+        clocks = B.ClockSampler(local, interval=0.02)
         ms, kernel_ms = _timed(sp, x_local, rope, B.SEQ, args.steps, args.warmup, clocks)
         status = _native.read_status(device)
 
