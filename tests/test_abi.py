@@ -87,3 +87,27 @@ def test_ring_entry_rejects_bad_arguments_before_any_device_call(lib):
     assert call(kv_seg_len=0) == -2
     assert call(kv_lens=big) == -2          # a segment longer than its slot
     assert call(out=None) == -1             # BF16 output requested, no destination
+
+
+def test_scatter_linear_rejects_bad_layouts_before_any_device_call(lib):
+    """Layout errors of erd_linear_bf16_scatter come back as the documented
+    codes (-1 null pointer, -2 bad shape, -3 misaligned) before the device is
+    touched."""
+    from eraserdit_b200 import _native
+    fn = lib.erd_linear_bf16_scatter
+    fn.argtypes = _native.SIGNATURES["erd_linear_bf16_scatter"]
+    fn.restype = ctypes.c_int
+    four = (ctypes.c_void_p * 4)(*([1 << 20] * 4))
+
+    def call(col0=4096, dests=four, ndest=4, group=512, rows=64, bs=256, ts=1536, m=128):
+        return fn(1 << 20, 2048, 1 << 20, 2048, None, 1 << 20, 6144, m, 6144, 2048, col0,
+                  dests, ndest, group, rows, bs, ts, None, None)
+
+    assert call(dests=None) == -1
+    assert call(group=384) == -2           # not a power of two
+    assert call(group=64, ndest=32) == -2   # narrower than 128 columns, more than 16 groups
+    assert call(ndest=3) == -2             # 3 x 512 columns do not cover n - col0
+    assert call(col0=4000) == -2           # not a multiple of 256
+    assert call(rows=48) == -2             # m not a multiple of the rows per batch entry
+    assert call(ts=1537) == -3             # destination stride not 16-byte aligned
+    assert call(dests=(ctypes.c_void_p * 4)(1 << 20, 1 << 20, (1 << 20) + 2, 1 << 20)) == -3
