@@ -18,7 +18,7 @@ boundaries (``layers/operator_fusion/triton/rmsnorm_native.py:1-5,25-43``).
 ``torch.nn.RMSNorm`` of torch 2.11 rounds once instead of twice and is NOT used.
 
 Fixtures are small: selected token rows plus whole-tensor checksums.  The test
-regenerates the seeded inputs with ``oracle.inputs`` and compares.
+regenerates the seeded inputs with ``eraserdit_b200.synthetic`` and compares.
 """
 
 from __future__ import annotations
@@ -41,7 +41,7 @@ HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO))
 
-from oracle.inputs import CONFIG0, make_hidden, make_params  # noqa: E402
+from eraserdit_b200.synthetic import CONFIG0, make_hidden, make_params  # noqa: E402
 
 ROWS = list(range(0, 192, 24)) + [191]
 

@@ -68,7 +68,7 @@ def test_fp8_layer_and_ulysses():
     from eraserdit_b200.layer import EraserDiTSelfAttention
     from eraserdit_b200.rotary import LTXVideoRotaryPosEmbed
     from eraserdit_b200.ulysses import emulate_ranks
-    from oracle.inputs import make_params
+    from eraserdit_b200.synthetic import make_params
     p = make_params(5, 1e-6, device="cuda").to(torch.bfloat16)
     bf16 = EraserDiTSelfAttention.from_params(p, device="cuda")
     fp8 = EraserDiTSelfAttention.from_params(p, device="cuda", precision="fp8")

@@ -4,7 +4,7 @@ import pytest
 import torch
 
 from oracle import reference_path as ref
-from oracle.inputs import CONFIG0, CONFIG1, LayerConfig, make_hidden, make_params
+from eraserdit_b200.synthetic import CONFIG0, CONFIG1, LayerConfig, make_hidden, make_params
 from tests.helpers import attention_fp32, cosine, max_abs
 
 pytestmark = pytest.mark.gpu

@@ -4,7 +4,7 @@ import pytest
 import torch
 
 from oracle import reference_path as ref
-from oracle.inputs import CONFIG0, make_hidden, make_params
+from eraserdit_b200.synthetic import CONFIG0, make_hidden, make_params
 
 ROWS = list(range(0, 192, 24)) + [191]
 

@@ -3,7 +3,7 @@ import pytest
 import torch
 
 from oracle import reference_path as ref
-from oracle.inputs import CONFIG0, CONFIG1
+from eraserdit_b200.synthetic import CONFIG0, CONFIG1
 from tests.helpers import bf16_ulp_distance
 
 pytestmark = pytest.mark.gpu

@@ -68,7 +68,7 @@ def test_piece_rejects_foreign_state_and_small_buffer():
 def _setup(frames, height, width, batch, seed):
     from eraserdit_b200.layer import EraserDiTSelfAttention
     from eraserdit_b200.rotary import LTXVideoRotaryPosEmbed
-    from oracle.inputs import make_params
+    from eraserdit_b200.synthetic import make_params
     p = make_params(seed, 1e-6, random_norm_weight=True, device="cuda")
     layer = EraserDiTSelfAttention.from_params(p.to(torch.bfloat16), device="cuda")
     rope = LTXVideoRotaryPosEmbed()(frames, height, width)

@@ -34,7 +34,7 @@ def _rank(rank, world, port, out_dir):
         from eraserdit_b200.rotary import LTXVideoRotaryPosEmbed
         from eraserdit_b200.topology import DiTGroups, DiTTopology
         from eraserdit_b200.ulysses import UlyssesSelfAttention, peer_exchange
-        from oracle.inputs import make_params
+        from eraserdit_b200.synthetic import make_params
         ring = 2
         topo = DiTTopology(ulysses=world // ring, ring=ring)
         groups = DiTGroups(topo)

@@ -3,7 +3,7 @@ NCCL path, chunks exchanged by copies) against the single-GPU layer output."""
 import pytest
 import torch
 
-from oracle.inputs import make_params
+from eraserdit_b200.synthetic import make_params
 from tests.helpers import cosine, max_abs
 
 pytestmark = pytest.mark.gpu

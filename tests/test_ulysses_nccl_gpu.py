@@ -30,7 +30,7 @@ def _rank(rank, world, port, out_dir):
         from eraserdit_b200.rotary import LTXVideoRotaryPosEmbed
         from eraserdit_b200.topology import DiTGroups, DiTTopology
         from eraserdit_b200.ulysses import UlyssesSelfAttention, peer_exchange
-        from oracle.inputs import make_params
+        from eraserdit_b200.synthetic import make_params
         groups = DiTGroups(DiTTopology(ulysses=world))
         group, ranks, index = groups.get("ulysses")
         p = make_params(3, 1e-6, random_norm_weight=True, device=device)
